@@ -1,0 +1,177 @@
+/*
+ * ragrt_b200.h -- C ABI of the B200-native (sm_100a) `weft` search path.
+ *
+ * Plain pointers, sizes and an opaque index handle; no C++ or torch types.  Every
+ * pointer argument named d_* is a device pointer on the calling thread's current CUDA
+ * device; `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * Every entry point returns 0 on success or a negative RAGRT_ERR_* code, with a
+ * readable message available from ragrt_last_error() (thread-local).  Nothing is
+ * silently truncated: a capacity or argument problem is an error.
+ *
+ * Work is enqueued on `stream`; entry points do not synchronise the host except
+ * ragrt_index_create (one synchronisation at the end of its validation) and
+ * ragrt_index_stats.
+ */
+#ifndef RAGRT_B200_H
+#define RAGRT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RAGRT_OK                0
+#define RAGRT_ERR_ARG          -1   /* bad argument (shape, range, alignment, null pointer)  */
+#define RAGRT_ERR_CUDA         -2   /* a CUDA runtime call failed                             */
+#define RAGRT_ERR_CAPACITY     -3   /* a size exceeds a documented limit                      */
+#define RAGRT_ERR_INDEX        -4   /* the bound arrays are not a valid plain-IVF index       */
+#define RAGRT_ERR_UNSUPPORTED  -5   /* a configuration outside the weft path                  */
+#define RAGRT_ERR_DEVICE       -6   /* called on a different device than the index's          */
+
+/* Limits of this build. */
+#define RAGRT_DIM              128  /* embedding dimension (fixed by the 2-bit codec)         */
+#define RAGRT_QUERY_ROWS        32  /* query rows per query (Stage 4 reads all 32)            */
+#define RAGRT_MAX_PROBE        128  /* nprobe (nc) per query token                            */
+#define RAGRT_MAX_CANDIDATES 16384  /* ndocs (k_candidates) per query and shard               */
+
+typedef struct ragrt_index ragrt_index;
+
+/*
+ * The arrays CorrIndex3D::bind_index takes (reference src/optix_corr_torch_3d.cpp:453-488),
+ * in the plain-IVF layout of src/build_plain_ivf.py:28-68, :98-127.  The caller keeps
+ * ownership; the arrays must stay alive and unchanged while the index is used.
+ */
+typedef struct {
+    const int64_t*  csr_row_ptrs;     /* [32, num_centroids + 1]; rows 1-31 must be empty    */
+    const void*     csr_col_eids;     /* [num_lists] uint8 (eid_bytes 1) or uint16 (2)        */
+    int32_t         eid_bytes;
+    const int64_t*  csr_block_sums;   /* [ceil(num_lists / 128)]                              */
+    const uint16_t* csr_lengths;      /* [num_lists]                                          */
+    const uint8_t*  csr_packed_24;    /* [3 * num_postings] little-endian 24-bit pids         */
+    int64_t         num_lists;
+    int64_t         num_postings;
+    const int64_t*  doc_offsets;      /* [num_passages + 1]                                   */
+    const int32_t*  doc_lens;         /* [num_passages]                                       */
+    const int32_t*  codes;            /* [num_tokens]                                         */
+    const uint8_t*  residuals;        /* [num_tokens, 32], 16-byte aligned                    */
+    int64_t         num_tokens;
+    const void*     centroids;        /* fp16 [num_centroids, 128], 16-byte aligned           */
+    const void*     bucket_weights;   /* fp16 [4]                                             */
+    const uint8_t*  reversed_bit_map; /* [256]                                                */
+    const uint8_t*  decomp_table;     /* [256, 4]                                             */
+    const uint32_t* doc_predicates;   /* [num_passages]; may be NULL (no filters)             */
+    int32_t         num_passages;     /* N  (< 2^24)                                          */
+    int32_t         num_centroids;    /* NC                                                   */
+    int32_t         num_eids;         /* E: chunk ids enumerated per probed centroid          */
+} ragrt_index_desc;
+
+/*
+ * Validates the bound arrays and builds the index's derived device structures (per
+ * centroid posting ranges, per pid-range sub-list offsets, centroid norms).  Replaces
+ * CorrIndex3D::bind_index (optix_corr_torch_3d.cpp:453-488).  Synchronises `stream`.
+ */
+int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** out, void* stream);
+int ragrt_index_destroy(ragrt_index* index);
+
+/*
+ * Stage 2: centroid scores and per-token top-nprobe with missing-score imputation, for
+ * B queries at once.  Replaces weft_prep.native_prep (src/weft_prep.py:32-47), which the
+ * reference runs per query as a torch fp16 GEMM + topk.
+ *   d_Q [B, rows, 128] fp16; d_ntok [B] int32 tokens per query (NULL = rows for all);
+ *   d_C [NC, 128] fp16.
+ * Selects kk = min(nc + impute, NC) centroids per token by (fp16 score desc, centroid
+ * id asc); fp16 scores are the exact dot products rounded once (RNE).
+ *   d_topc [B, rows, ncol] int32 and d_scores [B, rows, ncol] f32 with ncol = min(nc, kk);
+ *   scores = float(v_j) - m_t when imputed (kk > nc) else float(v_j);
+ *   d_m [B, rows] f32 = float(v_nc) (may be NULL);
+ *   d_full16 [B, rows, NC] fp16 (may be NULL): every score (the compact=False form).
+ * Rows t >= ntok get topc = -1, scores = 0, m = 0.
+ */
+int ragrt_centroid_topk(const void* d_Q, const int32_t* d_ntok, int32_t B, int32_t rows,
+                        const void* d_C, int32_t NC, int32_t nc, int32_t impute,
+                        int32_t* d_topc, float* d_scores, float* d_m, void* d_full16, void* stream);
+
+/*
+ * Stages 1-3 in `weft` mode for B queries: every chunk (eid < n_eids) of every probed
+ * centroid whose base score is > 0, per (passage, token) the max fp16 base score, per
+ * passage the sum over tokens, then candidate selection.  Replaces the all-codewords
+ * Stage 1 + ragrt_stage2 + ragrt_stage3_sparse + torch::topk of CorrIndex3D::stages23
+ * (optix_corr_torch_3d.cpp:558-594; ragrt_fused_kernel.cu:64-263, :343-431, :1038-1157).
+ *   d_topc [B, rows, kc] int32, d_scores f32: [B, rows, kc] (full_scores = 0, compact)
+ *   or [B, rows, NC] (full_scores = 1); d_ntok [B] (NULL = rows); d_masks [B] uint32
+ *   filter per query (NULL = none; a passage passes if (pred & mask) != 0).
+ *   K <= RAGRT_MAX_CANDIDATES candidates per query:
+ *   d_cand_pids [B, K] int32 (-1 padding), d_cand_sums [B, K] f32 (-inf padding),
+ *   d_num_touched [B] int64 (may be NULL): passages touched (U).
+ * Order: U <= K -> ascending pid; otherwise (sum desc, pid asc).  Sums are exact sums
+ * of the fp16 maxima rounded once to fp32.
+ */
+int ragrt_weft_candidates(ragrt_index* index, const int32_t* d_topc, const float* d_scores,
+                          int32_t full_scores, const int32_t* d_ntok, int32_t B, int32_t rows,
+                          int32_t kc, int32_t n_eids, const uint32_t* d_masks, int32_t K,
+                          int32_t* d_cand_pids, float* d_cand_sums, int64_t* d_num_touched,
+                          void* stream);
+
+/*
+ * Stage 4: fused 2-bit residual decompression + TileMaxSim for B queries with n
+ * candidates each.  Replaces launch_tile_maxsim_fused_decomp / native_tile_maxsim_fused_decomp
+ * (tile_maxsim_fused_decomp.cu:125-251, optix_corr_torch_3d.cpp:865-883).
+ *   d_Q [B, 32, 128] fp16, d_pids [B, n] int32 -> d_out [B, n] f32;
+ *   score = sum over the 32 query rows of the max over the passage's tokens of
+ *   q . d / |d|, d = fp16 add of centroid and bucket weight.  pid < 0 or >= N -> -inf;
+ *   a passage with no tokens -> 32 * -1e9.
+ *   mode 1: tensor-core kernel (tcgen05; the reference's "wmma" mode);
+ *   mode 0: CUDA-core kernel (the reference's "simt" mode).
+ */
+int ragrt_tile_maxsim(const void* d_Q, const int32_t* d_pids, int32_t B, int32_t n,
+                      const int64_t* d_doc_offsets, const int32_t* d_doc_lens, int32_t num_passages,
+                      const int32_t* d_codes, const uint8_t* d_residuals, const void* d_centroids,
+                      const void* d_bucket_weights, const uint8_t* d_reversed_bit_map,
+                      const uint8_t* d_decomp_table, float* d_out, int32_t mode, void* stream);
+
+/*
+ * Final filter + top-k per query: a candidate whose pid is < 0 or fails the query's mask
+ * scores -inf (ragrt_fused_kernel.cu:621-640), then the k best by (score desc, pid asc)
+ * (optix_corr_torch_3d.cpp:603-606).  d_preds [num_preds] may be NULL (no filters); a
+ * pid >= num_preds scores -inf when predicates are given.
+ *   d_pids/d_scores [B, n]; k <= n -> d_out_ids [B, k] int32, d_out_scores [B, k] f32
+ *   (may be NULL).
+ */
+int ragrt_final_topk(const int32_t* d_pids, const float* d_scores, int32_t B, int32_t n,
+                     const uint32_t* d_preds, int32_t num_preds, const uint32_t* d_masks, int32_t k,
+                     int32_t* d_out_ids, float* d_out_scores, void* stream);
+
+/*
+ * The whole `weft` search for a batch: Stage 2 -> Stages 1-3 -> Stage 4 -> final top-k,
+ * with no host synchronisation.  The batched entry the reference lacks (it loops over
+ * queries in CorrIndex3D::search_batch_pipelined, optix_corr_torch_3d.cpp:667-723).
+ *   d_Q [B, 32, 128] fp16, d_ntok [B] (NULL = 32), d_masks [B] (NULL = none),
+ *   nc probes per token, K candidates, k_top results, rerank_mode as ragrt_tile_maxsim.
+ *   d_out_ids [B, k_top] int32 (-1 padding), d_out_scores [B, k_top] f32 (may be NULL).
+ */
+int ragrt_weft_search(ragrt_index* index, const void* d_Q, const int32_t* d_ntok, int32_t B,
+                      int32_t nc, int32_t n_eids, const uint32_t* d_masks, int32_t K, int32_t k_top,
+                      int32_t rerank_mode, int32_t* d_out_ids, float* d_out_scores, void* stream);
+
+/*
+ * Counters accumulated over calls since the last reset (the reference's drop stats,
+ * ragrt_fused_kernel.cu:33-47, :884-899): out[0] queries, out[1] postings scanned
+ * (sum over kept (token, probe) pairs of list length), out[2] distinct postings read
+ * (each probed list once per query), out[3] passages touched, out[4] kept probes,
+ * out[5] candidates reranked.  Synchronises the device.
+ */
+#define RAGRT_NUM_STATS 6
+int ragrt_index_stats(ragrt_index* index, uint64_t* out, int32_t reset);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* ragrt_last_error(void);
+
+/* Library version string. */
+const char* ragrt_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RAGRT_B200_H */

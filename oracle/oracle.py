@@ -215,6 +215,8 @@ def ref_lib():
                                           C.POINTER(C.c_longlong), P]
         L.ref_tile_maxsim.restype = None
         L.ref_tile_maxsim.argtypes = [P, P, P, P, C.c_int, P, P, P, P, P, P, P, C.c_int, P]
+        L.ref_copy_d2d.restype = C.c_int
+        L.ref_copy_d2d.argtypes = [P, P, C.c_size_t]
         L.ref_mask_failing.restype = None
         L.ref_mask_failing.argtypes = [P, C.c_int, P, C.c_uint32, P, P]
         _ref = L

@@ -74,3 +74,8 @@ extern "C" void ref_stats(int enable, int reset, unsigned long long* out12) {
     if (reset) ragrt_reset_drop_stats();
     if (out12) ragrt_drop_stats(out12);
 }
+
+// device-to-device copy out of the reference-owned Stage-3 buffers (test convenience)
+extern "C" int ref_copy_d2d(void* dst, const void* src, size_t bytes) {
+    return (int)cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToDevice);
+}

@@ -1,0 +1,370 @@
+// s3_aggregate.cu -- Stages 1-3 of the reference in `weft` mode (all-codewords Stage 1,
+// codeword weight 0): for every query token t and probed centroid c_tj whose base score
+// (the imputation-shifted centroid score) is > 0, every posting of c_tj contributes
+// fp16(base) to (pid, t); a passage's score is the sum over tokens of its per-token max.
+// Reference: ragrt_fused_kernel.cu:64-263 (task collection, MIN_BASE_SCORE :206),
+// :343-392 (expand, filter :387, fp16 key :366), :403-431 + :1120-1156 (max per
+// (pid, token), sum per pid), optix_corr_torch_3d.cpp:569-585 (top-k candidates).
+//
+// B200 design (no sort, no host synchronisation):
+//   * The pid space is cut into ranges of W = 2^w_shift passages.  A CTA owns one
+//     (query, range) tile and keeps, per passage of the range, a 64-bit accumulator in
+//     shared memory: (sum of fp16 maxima in units of 2^-24) << 6 | (number of tokens).
+//   * A warp processes one query token at a time.  Its probes are sorted by score
+//     (native_prep returns them best first), so the FIRST probe of token t that holds a
+//     passage carries that token's max: a per-warp "seen" bitmap over the range marks
+//     (passage, t); duplicates inside one 32-posting chunk are resolved with
+//     __match_any_sync in favour of the lowest lane (= the better probe).
+//   * The posting sub-list of centroid c that falls in range r is read directly through
+//     the index's range-offset table (boff), coalesced, once per (token, probe).
+//   * Touched passages are emitted as 64-bit ranking keys into a per-query pool; a
+//     per-query CTA then selects the K candidates exactly (radix select + bitonic sort).
+// Sums are exact (fixed point) and rounded once to fp32; ties in candidate selection go to
+// the lower pid.
+#include <algorithm>
+
+#include "common.cuh"
+#include "index.cuh"
+#include "s3_common.cuh"
+
+namespace ragrt {
+
+constexpr int kS3Warps = 8;
+constexpr int kS3Threads = kS3Warps * 32;
+
+struct S3Params {
+    // index
+    const uint8_t* packed;
+    const uint32_t* preds;
+    const int64_t* rp;
+    const int64_t* list_off;
+    const int64_t* cstart;
+    const int32_t* clists;
+    const uint32_t* boff;
+    int N, NC, R, w_shift, n_eids;
+    // queries
+    const int32_t* topc;
+    const float* scores;
+    int full_scores, rows, kc;
+    const int32_t* ntok;
+    const uint32_t* masks;
+    int q0, nq;                  // queries [q0, q0 + nq) of the batch
+    // output
+    uint64_t* pool;              // [nq][pool_cap]
+    int64_t pool_cap;
+    unsigned long long* pool_count;   // [nq]
+    unsigned int* work;          // work counter
+    unsigned long long* stats;
+};
+
+__device__ __forceinline__ uint16_t f2h_pos15(float base) {
+    return (uint16_t)(__half_as_ushort(__float2half_rn(base)) & 0x7FFF);   // ragrt_fused_kernel.cu:366
+}
+
+__global__ void __launch_bounds__(kS3Threads)
+s3_accumulate(S3Params p) {
+    extern __shared__ __align__(16) unsigned char s3_smem[];
+    const int W = 1 << p.w_shift;
+    unsigned long long* sums = reinterpret_cast<unsigned long long*>(s3_smem);          // [W]
+    uint32_t* seen = reinterpret_cast<uint32_t*>(sums + W);                              // [warps][W/32]
+    uint16_t* touched = reinterpret_cast<uint16_t*>(seen + kS3Warps * (W >> 5));         // [W]
+    int32_t* pc = reinterpret_cast<int32_t*>(touched + W);                               // [32][kc]
+    uint16_t* pv = reinterpret_cast<uint16_t*>(pc + kRows * p.kc);                       // [32][kc]
+    __shared__ int s_np[kRows];
+    __shared__ unsigned s_ntouched;
+    __shared__ unsigned s_unit;
+    __shared__ unsigned long long s_base;
+
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+    uint32_t* my_seen = seen + w * (W >> 5);
+    for (int i = tid; i < W; i += kS3Threads) sums[i] = 0ull;
+    for (int i = tid; i < kS3Warps * (W >> 5); i += kS3Threads) seen[i] = 0u;
+    if (tid == 0) s_ntouched = 0;
+    unsigned long long st_post = 0, st_probes = 0;
+    int cached_q = -1;
+    const unsigned total_units = (unsigned)p.nq * (unsigned)p.R;
+    __syncthreads();
+
+    for (;;) {
+        if (tid == 0) s_unit = atomicAdd(p.work, 1u);
+        __syncthreads();
+        const unsigned unit = s_unit;
+        if (unit >= total_units) break;
+        const int qi = (int)(unit / p.R), r = (int)(unit % p.R);
+        const int q = p.q0 + qi;
+        const uint32_t mask = p.masks ? p.masks[q] : 0u;
+        const int nt = p.ntok ? min(p.ntok[q], p.rows) : p.rows;
+
+        // ---- kept probes of query q (warp t handles token t)
+        if (q != cached_q) {
+            for (int t = w; t < kRows; t += kS3Warps) {
+                int n = 0;
+                if (t < nt) {
+                    for (int j0 = 0; j0 < p.kc; j0 += 32) {
+                        int j = j0 + lane;
+                        int c = -1;
+                        float base = 0.f;
+                        if (j < p.kc) {
+                            c = p.topc[((int64_t)q * p.rows + t) * p.kc + j];
+                            if (c >= 0 && c < p.NC)
+                                base = p.full_scores ? p.scores[((int64_t)q * p.rows + t) * p.NC + c]
+                                                     : p.scores[((int64_t)q * p.rows + t) * p.kc + j];
+                        }
+                        bool keep = c >= 0 && c < p.NC && base > 0.0f;     // MIN_BASE_SCORE
+                        unsigned bal = __ballot_sync(0xFFFFFFFFu, keep);
+                        if (keep) {
+                            int slot = n + __popc(bal & ((1u << lane) - 1));
+                            pc[t * p.kc + slot] = c;
+                            pv[t * p.kc + slot] = f2h_pos15(base);
+                        }
+                        n += __popc(bal);
+                    }
+                }
+                if (lane == 0) s_np[t] = n;
+            }
+            cached_q = q;
+            __syncthreads();
+        }
+
+        // ---- accumulate: warp w takes tokens w, w + warps, ...
+        const int64_t range_lo = (int64_t)r << p.w_shift;
+        for (int t = w; t < nt; t += kS3Warps) {
+            const int np = s_np[t];
+            if (np == 0) continue;
+            if (lane == 0) st_probes += (unsigned long long)(r == 0 ? np : 0);
+            // probes are handled in groups of 32 (one per lane); np <= kc <= 128
+            for (int g0 = 0; g0 < np; g0 += 32) {
+                const int j = g0 + lane;
+                int64_t start = 0;
+                int len = 0;
+                uint16_t v = 0;
+                if (j < np) {
+                    const int c = pc[t * p.kc + j];
+                    v = pv[t * p.kc + j];
+                    const int nl = min(p.clists[c], p.n_eids);
+                    const int64_t cs = p.cstart[c];
+                    const int64_t cnt = nl > 0 ? p.list_off[p.rp[c] + nl] - cs : 0;
+                    const uint32_t* bo = p.boff + (int64_t)c * (p.R + 1) + r;
+                    const int64_t hi = (int64_t)bo[1] < cnt ? (int64_t)bo[1] : cnt;
+                    const int64_t lo = (int64_t)bo[0] < hi ? (int64_t)bo[0] : hi;
+                    start = cs + lo;
+                    len = (int)(hi - lo);
+                }
+                // inclusive scan of len over the group
+                int incl = len;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+                const int excl = incl - len;
+                st_post += (unsigned long long)len;
+                for (int e0 = 0; e0 < total; e0 += 32) {
+                    const int e = e0 + lane;
+                    // source probe: the last lane whose exclusive prefix is <= e
+                    int src = 0;
+#pragma unroll
+                    for (int step = 16; step; step >>= 1) {
+                        int cand = src + step;
+                        int ex = __shfl_sync(0xFFFFFFFFu, excl, cand & 31);
+                        if (cand < 32 && ex <= e) src = cand;
+                    }
+                    const int ex_src = __shfl_sync(0xFFFFFFFFu, excl, src);
+                    const int64_t st_src = __shfl_sync(0xFFFFFFFFu, start, src);
+                    const uint16_t v_src = (uint16_t)__shfl_sync(0xFFFFFFFFu, (int)v, src);
+                    bool ok = e < total;
+                    int local = -1;
+                    if (ok) {
+                        const int32_t pid = load_pid24(p.packed, st_src + (e - ex_src));
+                        local = (int)(pid - range_lo);
+                        ok = pid < p.N && local >= 0 && local < W;
+                        if (ok && mask) ok = (p.preds[pid] & mask) != 0u;   // ragrt_fused_kernel.cu:387
+                    }
+                    const int key = ok ? local : (0x40000000 | lane);
+                    const unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
+                    if (ok && lane == __ffs(peers) - 1) {
+                        const uint32_t bit = 1u << (local & 31);
+                        const uint32_t old = atomicOr(&my_seen[local >> 5], bit);
+                        if (!(old & bit)) {
+                            const unsigned long long add = (h_fixed24(v_src) << 6) | 1ull;
+                            const unsigned long long prev = atomicAdd(&sums[local], add);
+                            if (prev == 0ull) touched[atomicAdd(&s_ntouched, 1u)] = (uint16_t)local;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            for (int i = lane; i < (W >> 5); i += 32) my_seen[i] = 0u;
+            __syncwarp();
+        }
+        __syncthreads();
+
+        // ---- emit touched passages of this tile into the query's pool
+        const unsigned nt_touched = s_ntouched;
+        if (tid == 0 && nt_touched) s_base = atomicAdd(&p.pool_count[qi], (unsigned long long)nt_touched);
+        __syncthreads();
+        uint64_t* pool = p.pool + (int64_t)qi * p.pool_cap;
+        for (unsigned i = tid; i < nt_touched; i += kS3Threads) {
+            const int local = touched[i];
+            const unsigned long long acc = sums[local];
+            sums[local] = 0ull;
+            const float s = __ull2float_rn(acc >> 6) * 0x1p-24f;
+            pool[s_base + i] = rank_key(s, (int32_t)(range_lo + local));
+        }
+        __syncthreads();
+        if (tid == 0) s_ntouched = 0;
+    }
+    // stats: postings scanned (per kept probe, whole list), kept probes
+    for (int o = 16; o; o >>= 1) {
+        st_post += __shfl_xor_sync(0xFFFFFFFFu, st_post, o);
+        st_probes += __shfl_xor_sync(0xFFFFFFFFu, st_probes, o);
+    }
+    if (lane == 0 && p.stats) {
+        atomicAdd(&p.stats[1], st_post);
+        atomicAdd(&p.stats[4], st_probes);
+    }
+}
+
+// per query: distinct probed lists and their postings (the roofline's P_lists)
+__global__ void s3_query_lists(S3Params p, unsigned long long* __restrict__ distinct_postings) {
+    __shared__ int s_ids[kRows * RAGRT_MAX_PROBE];
+    __shared__ unsigned s_n;
+    const int q = p.q0 + blockIdx.x;
+    const int nt = p.ntok ? min(p.ntok[q], p.rows) : p.rows;
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * p.kc; i += blockDim.x) {
+        const int t = i / p.kc, j = i % p.kc;
+        const int c = p.topc[((int64_t)q * p.rows + t) * p.kc + j];
+        if (c < 0 || c >= p.NC) continue;
+        const float base = p.full_scores ? p.scores[((int64_t)q * p.rows + t) * p.NC + c]
+                                         : p.scores[((int64_t)q * p.rows + t) * p.kc + j];
+        if (base > 0.0f) s_ids[atomicAdd(&s_n, 1u)] = c;
+    }
+    __syncthreads();
+    const unsigned n = s_n;
+    unsigned long long tot = 0;
+    for (unsigned i = threadIdx.x; i < n; i += blockDim.x) {
+        const int c = s_ids[i];
+        bool first = true;
+        for (unsigned k = 0; k < i; ++k)
+            if (s_ids[k] == c) { first = false; break; }
+        if (first) {
+            const int nl = min(p.clists[c], p.n_eids);
+            tot += nl > 0 ? (unsigned long long)(p.list_off[p.rp[c] + nl] - p.cstart[c]) : 0ull;
+        }
+    }
+    for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
+    if ((threadIdx.x & 31) == 0 && tot) {
+        atomicAdd(&distinct_postings[blockIdx.x], tot);
+        if (p.stats) atomicAdd(&p.stats[2], tot);
+    }
+}
+
+}  // namespace ragrt
+
+using namespace ragrt;
+
+namespace ragrt {
+
+size_t s3_workspace_bytes(const ragrt_index* ix, int nq_sub) {
+    return sizeof(uint64_t) * (size_t)nq_sub * ix->d.num_passages        // pool
+           + sizeof(unsigned long long) * (size_t)nq_sub * 2            // pool counts, distinct postings
+           + 256;
+}
+
+int s3_max_sub_batch(const ragrt_index* ix, int B) {
+    // keep the candidate pool under ~2 GiB
+    int64_t per_q = (int64_t)ix->d.num_passages * 8;
+    int64_t sub = std::max<int64_t>(1, ((int64_t)2 << 30) / per_q);
+    return (int)std::min<int64_t>(sub, B);
+}
+
+int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_scores, const int32_t* ntok, int B,
+           int rows, int kc, int n_eids, const uint32_t* masks, int K, int32_t* cand_pids, float* cand_sums,
+           int64_t* num_touched, void* ws, size_t ws_bytes, cudaStream_t stream) {
+    const int sub = s3_max_sub_batch(ix, B);
+    const size_t need = s3_workspace_bytes(ix, sub);
+    if (ws_bytes < need) return fail(RAGRT_ERR_CAPACITY, "internal: stage-3 workspace %zu < %zu", ws_bytes, need);
+    const int W = 1 << ix->w_shift;
+    char* wsp = (char*)ws;
+    uint64_t* pool = (uint64_t*)wsp;
+    wsp += sizeof(uint64_t) * (size_t)sub * ix->d.num_passages;
+    unsigned long long* counts = (unsigned long long*)wsp;        // [sub] pool counts, [sub] distinct postings
+    wsp += sizeof(unsigned long long) * (size_t)sub * 2;
+    unsigned int* work = (unsigned int*)wsp;
+
+    const size_t smem = sizeof(unsigned long long) * W + sizeof(uint32_t) * kS3Warps * (W >> 5) +
+                        sizeof(uint16_t) * W + (sizeof(int32_t) + sizeof(uint16_t)) * kRows * kc + 16;
+    if (smem > 220 * 1024) return fail(RAGRT_ERR_CAPACITY, "stage-3 tile needs %zu bytes of shared memory", smem);
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s3_accumulate, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    RAGRT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, s3_accumulate, kS3Threads, smem));
+    per_sm = std::max(1, per_sm);
+    for (int q0 = 0; q0 < B; q0 += sub) {
+        const int nq = std::min(sub, B - q0);
+        RAGRT_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(unsigned long long) * 2 * sub + 16, stream));
+        S3Params p;
+        p.packed = ix->d.csr_packed_24;
+        p.preds = ix->d.doc_predicates;
+        p.rp = ix->d.csr_row_ptrs;
+        p.list_off = ix->list_off;
+        p.cstart = ix->cstart;
+        p.clists = ix->clists;
+        p.boff = ix->boff;
+        p.N = ix->d.num_passages;
+        p.NC = ix->d.num_centroids;
+        p.R = ix->num_ranges;
+        p.w_shift = ix->w_shift;
+        p.n_eids = n_eids;
+        p.topc = topc;
+        p.scores = scores;
+        p.full_scores = full_scores;
+        p.rows = rows;
+        p.kc = kc;
+        p.ntok = ntok;
+        p.masks = masks;
+        p.q0 = q0;
+        p.nq = nq;
+        p.pool = pool;
+        p.pool_cap = ix->d.num_passages;
+        p.pool_count = counts;
+        p.work = work;
+        p.stats = ix->stats;
+        if (masks && !ix->d.doc_predicates) p.masks = nullptr;   // no predicates bound: no filter
+        const int64_t units = (int64_t)nq * ix->num_ranges;
+        const int grid = (int)std::min<int64_t>(units, (int64_t)per_sm * num_sms());
+        s3_accumulate<<<grid, kS3Threads, smem, stream>>>(p);
+        RAGRT_LAUNCH_CHECK();
+        s3_query_lists<<<nq, 256, 0, stream>>>(p, counts + sub);
+        RAGRT_LAUNCH_CHECK();
+        int rc = s3_select_launch(pool, ix->d.num_passages, counts, q0, nq, K, cand_pids, cand_sums, num_touched,
+                                  ix->stats, stream);
+        if (rc) return rc;
+    }
+    return RAGRT_OK;
+}
+
+}  // namespace ragrt
+
+extern "C" int ragrt_weft_candidates(ragrt_index* ix, const int32_t* d_topc, const float* d_scores,
+                                     int32_t full_scores, const int32_t* d_ntok, int32_t B, int32_t rows,
+                                     int32_t kc, int32_t n_eids, const uint32_t* d_masks, int32_t K,
+                                     int32_t* d_cand_pids, float* d_cand_sums, int64_t* d_num_touched,
+                                     void* stream_) {
+    cudaStream_t stream = (cudaStream_t)stream_;
+    RAGRT_REQUIRE(ix && d_topc && d_scores && d_cand_pids && d_cand_sums, "null argument");
+    int rc = check_device(ix);
+    if (rc) return rc;
+    RAGRT_REQUIRE(B >= 1 && rows >= 1 && rows <= kRows, "B >= 1 and 1 <= rows <= 32 required");
+    RAGRT_REQUIRE(kc >= 1 && kc <= RAGRT_MAX_PROBE, "kc must be in [1, %d]", RAGRT_MAX_PROBE);
+    RAGRT_REQUIRE(K >= 1 && K <= RAGRT_MAX_CANDIDATES && K <= ix->d.num_passages,
+                  "K=%d must be in [1, min(N, %d)]", K, RAGRT_MAX_CANDIDATES);
+    RAGRT_REQUIRE(n_eids >= 1, "n_eids must be >= 1");
+    const int sub = s3_max_sub_batch(ix, B);
+    rc = ensure_workspace(ix, s3_workspace_bytes(ix, sub), stream);
+    if (rc) return rc;
+    return s3_run(ix, d_topc, d_scores, full_scores, d_ntok, B, rows, kc, n_eids, d_masks, K, d_cand_pids,
+                  d_cand_sums, d_num_touched, ix->ws.base, ix->ws.bytes, stream);
+}
