@@ -1,0 +1,442 @@
+#!/usr/bin/env python
+"""
+bench.py -- throughput of the B200 `weft` search path (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg3]
+
+One step = one batch of queries through the whole path (Stage 2 centroid scoring +
+top-nprobe, Stages 1-3 posting aggregation + candidate selection, Stage 4 fused
+decompress + TileMaxSim, final top-k).  The default workload is BASELINE config 3:
+2,000,000 synthetic passages (lengths U[60,180], mean 120), 65,536 fp16 centroids,
+2-bit residuals, batch 256 x 32 query tokens, nprobe 32, 4,096 candidates, top-10.
+Inputs are seeded synthetic data (ragrt_b200.synth) standing in for LoTTE / MS MARCO.
+
+Prints ONE JSON line on rank 0.  `value` is queries/s with inputs resident in HBM; `e2e`
+is the same through the public API with the query batch copied from pinned host memory
+and the results copied back inside every timed step.  `stages` and `roofline` come from a
+second timed pass that records CUDA events at the stage boundaries on the launching stream.
+
+Multi-GPU (--gpus N under torchrun): the corpus is sharded by contiguous pid ranges, every
+rank searches the same query batch against its shard (per-shard K = ceil(K / N)), and the
+per-shard top-k lists are merged with one NCCL all-gather.  Whole-job work is fixed
+("scaling": "strong").
+
+--impl reference times the CPU restatement of the reference path (oracle/, all host
+threads) on a bounded sample of the same workload, rank 0 only.
+"""
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "queries/s at 1/2/4/8 B200 (weft, batch 256, top-10); Stage-4 doc-tokens/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+CONFIGS = {
+    "cfg3": dict(num_docs=2_000_000, len_range=(60, 180), centres=1024, subs=64, batch=256, nc=32, K=4096,
+                 k_top=10, masks=None,
+                 desc="full weft, 2M docs (len U[60,180], mean 120), 65,536 fp16 centroids, 2-bit residuals, "
+                      "batch 256 x 32 tokens, nprobe 32, 4,096 candidates, top-10"),
+    "cfg4": dict(num_docs=2_000_000, len_range=(60, 180), centres=1024, subs=64, batch=256, nc=32, K=4096,
+                 k_top=10, masks=(1, 2, 4),
+                 desc="cfg3 + predicate filters inside Stage 3 (bits with selectivity 1%, 10%, 50%; "
+                      "queries cycle through the three masks)"),
+    "small": dict(num_docs=200_000, len_range=(60, 180), centres=1024, subs=64, batch=256, nc=32, K=4096,
+                  k_top=10, masks=None, desc="cfg3 at 1/10 of the corpus (quick runs)"),
+}
+
+
+# ----------------------------------------------------------------------------- helpers
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {k: float(d[k]) for k in FALLBACK_PEAKS if k in d}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.out.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = max(smax, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    if world != n_gpus:
+        log(f"note: --gpus {n_gpus} but WORLD_SIZE={world}; using {world}")
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- data
+def build_workload(cfg, rank, world, seed=0):
+    """Synthetic corpus (generated on the GPU) and this rank's shard of it."""
+    from ragrt_b200 import synth, index_build
+    t0 = time.time()
+    dev = "cuda"
+    centres, cents = synth.make_centroids(num_centres=cfg["centres"], subs=cfg["subs"], seed=seed, device=dev)
+    corp = synth.make_corpus(cfg["num_docs"], centres, cents, len_range=cfg["len_range"], seed=seed, device=dev)
+    preds = synth.make_predicates(cfg["num_docs"], seed=1, device=dev)
+    N = cfg["num_docs"]
+    lo = (N * rank) // world
+    hi = (N * (rank + 1)) // world
+    off = corp["doc_offsets"]
+    t_lo, t_hi = int(off[lo]), int(off[hi])
+    shard = {
+        "doclens": corp["doclens"][lo:hi].contiguous(),
+        "doc_offsets": (off[lo:hi + 1] - t_lo).contiguous(),
+        "codes": corp["codes"][t_lo:t_hi].contiguous(),
+        "residuals": corp["residuals"][t_lo:t_hi].contiguous(),
+        "preds": preds[lo:hi].contiguous(),
+        "pid_base": lo,
+    }
+    del corp["codes"], corp["residuals"]
+    torch.cuda.empty_cache()
+    ix = index_build.plain_ivf_index(shard["codes"], shard["doclens"], cents.shape[0])
+    log(f"[rank {rank}] corpus: {hi - lo:,} docs, {t_hi - t_lo:,} tokens, {ix['num_postings']:,} postings, "
+        f"E={ix['E']} ({time.time() - t0:.1f} s)")
+    return centres, cents, corp, shard, ix
+
+
+def make_index(cents, corp, shard, ix):
+    from ragrt_b200.weft import WeftIndex
+    return WeftIndex(ix["csr_row_ptrs"], ix["csr_col_eids"], ix["csr_block_sums"], ix["csr_lengths"],
+                     ix["csr_packed_24"], shard["doc_offsets"], shard["doclens"], shard["codes"], shard["residuals"],
+                     cents, corp["bucket_weights"], corp["reversed_bit_map"], corp["decomp_table"],
+                     doc_predicates=shard["preds"], num_passages=shard["doclens"].shape[0],
+                     num_centroids=cents.shape[0], E=ix["E"])
+
+
+# ----------------------------------------------------------------------------- reference arm (CPU)
+def host_oracle_index(cents, corp, shard, ix):
+    """Host copy of the bound index for the CPU restatement (oracle/)."""
+    from oracle import oracle as O
+    host = {
+        "csr_row_ptrs": ix["csr_row_ptrs"].cpu().numpy(), "csr_col_eids": ix["csr_col_eids"].cpu().numpy(),
+        "csr_block_sums": ix["csr_block_sums"].cpu().numpy(),
+        "csr_lengths": ix["csr_lengths"].cpu().view(torch.int16).numpy().view(np.uint16),
+        "csr_packed_24": ix["csr_packed_24"].cpu().numpy(), "doc_offsets": shard["doc_offsets"].cpu().numpy(),
+        "doc_lens": shard["doclens"].cpu().numpy(), "codes": shard["codes"].cpu().numpy(),
+        "residuals": shard["residuals"].cpu().numpy(), "centroids": cents.cpu().numpy(),
+        "bucket_weights": corp["bucket_weights"].cpu().numpy(),
+        "reversed_bit_map": corp["reversed_bit_map"].cpu().numpy(), "decomp_table": corp["decomp_table"].cpu().numpy(),
+        "doc_predicates": shard["preds"].cpu().to(torch.int64).numpy().astype(np.uint32),
+    }
+    return O.Index(host)
+
+
+def oracle_step(oix, cfg, E, Q, masks, sample, nthreads):
+    """The CPU restatement on `sample` queries of a batch; returns seconds."""
+    from oracle import oracle as O
+    q = Q[:sample].cpu().numpy()
+    mk = masks[:sample].cpu().numpy().astype(np.uint32) if masks is not None else None
+    t0 = time.time()
+    O.weft_search(oix, q, np.full(sample, 32, np.int32), cfg["nc"], int(E), mk, min(cfg["K"], oix.N),
+                  cfg["k_top"], nthreads=nthreads)
+    return time.time() - t0
+
+
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return 0
+    nthreads = os.cpu_count() or 1
+    centres, cents, corp, shard, ix = build_workload(cfg, 0, 1)
+    Qall = make_queries(centres, cfg, args.warmup + args.steps, 0)
+    sample = max(1, min(cfg["batch"], args.cpu_sample or nthreads))
+    masks = make_masks(cfg, sample)
+    oix = host_oracle_index(cents, corp, shard, ix)
+    for i in range(args.warmup):
+        oracle_step(oix, cfg, ix["E"], Qall[i], masks, sample, nthreads)
+    times = [oracle_step(oix, cfg, ix["E"], Qall[i], masks, sample, nthreads)
+             for i in range(args.warmup, args.warmup + args.steps)]
+    tot = sum(times)
+    v = sample * len(times) / tot
+    line = {"metric": METRIC, "value": v, "unit": "queries/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * tot / len(times),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16 in, exact/f64 (CPU)",
+            "data": "synthetic", "config": {"workload": f"{args.config}: {cfg['desc']}",
+                                           "sample_per_step": f"{sample} queries of a 256-query batch"},
+            "cpu_baseline": {"value": v, "unit": "queries/s", "cores": nthreads, "kind": "port",
+                             "sample": f"{sample} queries per step through all stages (oracle/weft_oracle.c, "
+                                       f"OpenMP over queries)"},
+            "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def make_queries(centres, cfg, nbatches, seed):
+    from ragrt_b200 import synth
+    Q = synth.make_queries(centres, nbatches * cfg["batch"], seed=1000 + seed)
+    return Q.view(nbatches, cfg["batch"], 32, 128)
+
+
+def make_masks(cfg, B):
+    if not cfg["masks"]:
+        return None
+    m = torch.tensor([cfg["masks"][i % len(cfg["masks"])] for i in range(B)], dtype=torch.int32, device="cuda")
+    return m
+
+
+# ----------------------------------------------------------------------------- ours
+def merge_shards(ids, sc, world, k_top, pid_base):
+    """All-gather per-shard top-k (score, global pid) and merge (score desc, pid asc)."""
+    import torch.distributed as dist
+    gpid = torch.where(ids >= 0, ids + pid_base, ids)
+    pack = torch.stack([sc, gpid.to(torch.float32)], 0)              # pids < 2^24: exact in fp32
+    out = torch.empty(world, *pack.shape, dtype=pack.dtype, device=pack.device)
+    dist.all_gather_into_tensor(out, pack)
+    scores = out[:, 0].permute(1, 0, 2).reshape(ids.shape[0], -1)
+    pids = out[:, 1].permute(1, 0, 2).reshape(ids.shape[0], -1).to(torch.int64)
+    key = torch.where(pids >= 0, pids, torch.full_like(pids, 1 << 40))
+    order = torch.argsort(key, dim=1, stable=True)                    # pid asc ...
+    scores, pids = torch.gather(scores, 1, order), torch.gather(pids, 1, order)
+    order = torch.argsort(scores, dim=1, descending=True, stable=True)  # ... then score desc
+    return torch.gather(pids, 1, order)[:, :k_top], torch.gather(scores, 1, order)[:, :k_top]
+
+
+def run_ours(args, cfg, rank, world, local):
+    from ragrt_b200 import _lib
+    centres, cents, corp, shard, ix = build_workload(cfg, rank, world)
+    wix = make_index(cents, corp, shard, ix)
+    nb = args.warmup + args.steps
+    Q = make_queries(centres, cfg, nb, 0)
+    B, nc, k_top = cfg["batch"], cfg["nc"], cfg["k_top"]
+    K = min(int(math.ceil(cfg["K"] / world)), wix.N)
+    masks = make_masks(cfg, B)
+    ids = torch.empty(nb, B, k_top, dtype=torch.int32, device="cuda")
+    sc = torch.empty(nb, B, k_top, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        wix.search(Q[i], nc=nc, K=K, k_top=k_top, masks=masks, out=(ids[i], sc[i]))
+        if world > 1:
+            merge_shards(ids[i], sc[i], world, k_top, shard["pid_base"])
+
+    # ---- warm-up, then the timed region (inputs resident in HBM, a new query batch per step)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    wix.stats(reset=True)
+    l0 = _lib.lib().ragrt_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record(stream)
+        for i in range(args.warmup, nb):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = _lib.lib().ragrt_launch_count() - l0
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    value = B * args.steps / (ms / 1000.0)
+    stats = wix.stats()
+
+    # ---- end to end through the public API: pinned host queries in, results out, every step
+    Qh = Q.cpu().pin_memory()
+    Qd = torch.empty_like(Q[0])
+    ids_h = torch.empty(nb, B, k_top, dtype=torch.int32).pin_memory()
+    sc_h = torch.empty(nb, B, k_top, dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for i in range(args.warmup, nb):
+        Qd.copy_(Qh[i], non_blocking=True)
+        o_ids, o_sc = wix.search(Qd, nc=nc, K=K, k_top=k_top, masks=masks)
+        if world > 1:
+            o_ids, o_sc = merge_shards(o_ids, o_sc, world, k_top, shard["pid_base"])
+        ids_h[i].copy_(o_ids.to(torch.int32), non_blocking=True)
+        sc_h[i].copy_(o_sc, non_blocking=True)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3), world)
+    e2e = B * args.steps / (ms_e2e / 1000.0)
+
+    # ---- stage breakdown: events at the stage boundaries on the launching stream
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    cand_tokens = 0
+    wix.stats(reset=True)
+    torch.cuda.synchronize()
+    for j, i in enumerate(range(args.warmup, nb)):
+        wix.search_profiled(Q[i], ev[j], nc=nc, K=K, k_top=k_top, masks=masks, out=(ids[i], sc[i]))
+    torch.cuda.synchronize()
+    st2 = wix.stats()
+    stage_ms = np.array([[ev[j][s].elapsed_time(ev[j][s + 1]) for s in range(4)] for j in range(args.steps)])
+    stage_ms = stage_ms.mean(0)
+    # Stage-4 algorithmic work: candidates and their tokens (one query batch, same K)
+    topc, s2sc, _, _ = wix.centroid_topk(Q[args.warmup], nc)
+    cp, _, _ = wix.candidates(topc, s2sc, K, masks=masks)
+    valid = cp >= 0
+    cand_tokens = int(wix.doc_lens[cp[valid].long()].sum())
+    n_cand = int(valid.sum())
+    peaks, peak_kind = load_peaks()
+    s2_flops = 2.0 * B * 32 * wix.NC * 128
+    s3_bytes = (3.0 * st2["distinct_postings"] + 8.0 * st2["touched"]) / args.steps
+    s4_bytes = 36.0 * cand_tokens + 16.0 * n_cand
+    stages = {
+        "s2_centroid_topk": {"ms": stage_ms[0], "achieved": s2_flops / (stage_ms[0] / 1e3) / 1e12,
+                             "unit": "TFLOP/s", "peak": peaks["bf16_tflops"], "bound": "tensor",
+                             "work": f"{s2_flops / 1e9:.1f} GFLOP/step"},
+        "s3_aggregate": {"ms": stage_ms[1], "achieved": s3_bytes / (stage_ms[1] / 1e3) / 1e9, "unit": "GB/s",
+                         "peak": peaks["hbm_gbs"], "bound": "hbm",
+                         "work": f"{s3_bytes / 1e6:.1f} MB/step (3 B x distinct postings + 8 B x touched)"},
+        "s4_maxsim": {"ms": stage_ms[2], "achieved": s4_bytes / (stage_ms[2] / 1e3) / 1e9, "unit": "GB/s",
+                      "peak": peaks["hbm_gbs"], "bound": "hbm",
+                      "work": f"{s4_bytes / 1e6:.1f} MB/step (36 B x {cand_tokens:,} doc tokens + 16 B x cand)",
+                      "doc_tokens_per_s": cand_tokens / (stage_ms[2] / 1e3)},
+        "final_topk": {"ms": stage_ms[3]},
+    }
+    for s in stages.values():
+        if "achieved" in s:
+            s["frac"] = s["achieved"] / s["peak"]
+    dom = max(("s2_centroid_topk", "s3_aggregate", "s4_maxsim"), key=lambda k: stages[k]["ms"])
+    d = stages[dom]
+    roofline = {"bound": d["bound"], "achieved": d["achieved"], "peak": d["peak"], "unit": d["unit"],
+                "frac": d["frac"], "traffic": None, "kernel": dom, "peak_source": peak_kind}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        nthreads = os.cpu_count() or 1
+        sample = max(1, min(B, args.cpu_sample or nthreads))
+        oix = host_oracle_index(cents, corp, shard, ix)
+        dt = oracle_step(oix, cfg, ix["E"], Q[args.warmup], masks, sample, nthreads)
+        cpu = {"value": sample / dt, "unit": "queries/s", "cores": nthreads, "kind": "port",
+               "sample": f"{sample} queries of one batch through all stages ({dt:.1f} s; oracle/weft_oracle.c, "
+                         f"OpenMP over queries)"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"{args.config}: {cfg['desc']}", "batch": B, "nprobe": nc,
+                       "candidates_per_shard": K, "top_k": k_top, "docs": cfg["num_docs"],
+                       "parallelism": f"doc-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (index ~9 GB) and a distinct query batch per step"},
+            "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": int(Q[0].numel() * 2),
+                    "d2h_bytes_per_step": int(B * k_top * 8)},
+            "roofline": roofline,
+            "stages": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()}
+                       for k, v in stages.items()},
+            "stage4_doc_tokens_per_s": stages["s4_maxsim"]["doc_tokens_per_s"],
+            "cpu_baseline": cpu,
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+            "counters": {k: int(v) for k, v in stats.items()},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg3")
+    ap.add_argument("--cpu-sample", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    cfg = CONFIGS[args.config]
+    rank, world, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        return run_reference(args, cfg, rank, world)
+    return run_ours(args, cfg, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -156,6 +156,18 @@ int ragrt_weft_search(ragrt_index* index, const void* d_Q, const int32_t* d_ntok
                       int32_t rerank_mode, int32_t* d_out_ids, float* d_out_scores, void* stream);
 
 /*
+ * ragrt_weft_search with stage timing: records events[0..4] (cudaEvent_t, created by the
+ * caller; NULL entries skipped) on `stream` before Stage 2, after Stage 2, after Stages 1-3,
+ * after Stage 4 and after the final top-k.  The counterpart of the reference's
+ * CorrIndex3D::search_single_query_profiled (optix_corr_torch_3d.cpp:638-665), without
+ * its host synchronisation.
+ */
+int ragrt_weft_search_profiled(ragrt_index* index, const void* d_Q, const int32_t* d_ntok, int32_t B,
+                               int32_t nc, int32_t n_eids, const uint32_t* d_masks, int32_t K, int32_t k_top,
+                               int32_t rerank_mode, int32_t* d_out_ids, float* d_out_scores,
+                               void* const* events, void* stream);
+
+/*
  * Counters accumulated over calls since the last reset (the reference's drop stats,
  * ragrt_fused_kernel.cu:33-47, :884-899): out[0] queries, out[1] postings scanned
  * (sum over kept (token, probe) pairs of list length), out[2] distinct postings read
@@ -167,6 +179,9 @@ int ragrt_index_stats(ragrt_index* index, uint64_t* out, int32_t reset);
 
 /* Message of the last failing call on this thread ("" if none). */
 const char* ragrt_last_error(void);
+
+/* Number of kernels this library has launched in the process (all entry points). */
+uint64_t ragrt_launch_count(void);
 
 /* Library version string. */
 const char* ragrt_version(void);

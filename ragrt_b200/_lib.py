@@ -42,9 +42,11 @@ _SIGS = {
     "ragrt_tile_maxsim": (I32, [P, P, I32, I32, P, P, I32, P, P, P, P, P, P, P, I32, P]),
     "ragrt_final_topk": (I32, [P, P, I32, I32, P, I32, P, I32, P, P, P]),
     "ragrt_weft_search": (I32, [P, P, P, I32, I32, I32, P, I32, I32, I32, P, P, P]),
+    "ragrt_weft_search_profiled": (I32, [P, P, P, I32, I32, I32, P, I32, I32, I32, P, P, P, P]),
     "ragrt_index_stats": (I32, [P, C.POINTER(C.c_uint64), I32]),
     "ragrt_last_error": (C.c_char_p, []),
     "ragrt_version": (C.c_char_p, []),
+    "ragrt_launch_count": (C.c_uint64, []),
 }
 
 _lib = None

@@ -45,10 +45,13 @@ size_t weft_search_bytes(const ragrt_index* ix, int B, int nc, int K) {
 
 using namespace ragrt;
 
-extern "C" int ragrt_weft_search(ragrt_index* ix, const void* d_Q, const int32_t* d_ntok, int32_t B, int32_t nc,
-                                 int32_t n_eids, const uint32_t* d_masks, int32_t K, int32_t k_top,
-                                 int32_t rerank_mode, int32_t* d_out_ids, float* d_out_scores, void* stream_) {
-    cudaStream_t stream = (cudaStream_t)stream_;
+static int weft_search_impl(ragrt_index* ix, const void* d_Q, const int32_t* d_ntok, int32_t B, int32_t nc,
+                            int32_t n_eids, const uint32_t* d_masks, int32_t K, int32_t k_top, int32_t rerank_mode,
+                            int32_t* d_out_ids, float* d_out_scores, void* const* events, cudaStream_t stream) {
+    auto mark = [&](int i) -> int {
+        if (events && events[i]) RAGRT_CUDA_TRY(cudaEventRecord((cudaEvent_t)events[i], stream));
+        return RAGRT_OK;
+    };
     RAGRT_REQUIRE(ix && d_Q && d_out_ids, "null argument");
     int rc = check_device(ix);
     if (rc) return rc;
@@ -74,17 +77,35 @@ extern "C" int ragrt_weft_search(ragrt_index* ix, const void* d_Q, const int32_t
     const size_t s3b = s3_workspace_bytes(ix, sub);
     char* s3ws = c.take<char>(s3b);
 
+    if ((rc = mark(0))) return rc;
     rc = s2_run((const __half*)d_Q, d_ntok, B, kRows, (const __half*)ix->d.centroids, NC, nc, 1, topc, scores,
                 nullptr, nullptr, partial, stream);
-    if (rc) return rc;
+    if (rc || (rc = mark(1))) return rc;
     rc = s3_run(ix, topc, scores, 0, d_ntok, B, kRows, nc, std::min(n_eids, ix->d.num_eids), d_masks, K, cand, csum,
                 nullptr, s3ws, s3b, stream);
-    if (rc) return rc;
+    if (rc || (rc = mark(2))) return rc;
     S4Docs D{ix->d.doc_offsets, ix->d.doc_lens, ix->d.codes, ix->d.residuals, (const __half*)ix->d.centroids,
              (const __half*)ix->d.bucket_weights, ix->d.reversed_bit_map, ix->d.decomp_table, ix->d.num_passages};
     rc = rerank_mode == 1 ? s4_tc_launch((const __half*)d_Q, cand, B, K, D, fsc, stream)
                           : s4_simt_launch((const __half*)d_Q, cand, B, K, D, fsc, stream);
+    if (rc || (rc = mark(3))) return rc;
+    rc = final_topk_launch(cand, fsc, B, K, ix->d.doc_predicates, ix->d.num_passages, d_masks, k_top, d_out_ids,
+                           d_out_scores, stream);
     if (rc) return rc;
-    return final_topk_launch(cand, fsc, B, K, ix->d.doc_predicates, ix->d.num_passages, d_masks, k_top, d_out_ids,
-                             d_out_scores, stream);
+    return mark(4);
+}
+
+extern "C" int ragrt_weft_search(ragrt_index* ix, const void* d_Q, const int32_t* d_ntok, int32_t B, int32_t nc,
+                                 int32_t n_eids, const uint32_t* d_masks, int32_t K, int32_t k_top,
+                                 int32_t rerank_mode, int32_t* d_out_ids, float* d_out_scores, void* stream) {
+    return weft_search_impl(ix, d_Q, d_ntok, B, nc, n_eids, d_masks, K, k_top, rerank_mode, d_out_ids, d_out_scores,
+                            nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int ragrt_weft_search_profiled(ragrt_index* ix, const void* d_Q, const int32_t* d_ntok, int32_t B,
+                                          int32_t nc, int32_t n_eids, const uint32_t* d_masks, int32_t K,
+                                          int32_t k_top, int32_t rerank_mode, int32_t* d_out_ids,
+                                          float* d_out_scores, void* const* events, void* stream) {
+    return weft_search_impl(ix, d_Q, d_ntok, B, nc, n_eids, d_masks, K, k_top, rerank_mode, d_out_ids, d_out_scores,
+                            events, (cudaStream_t)stream);
 }

@@ -11,6 +11,7 @@ namespace ragrt {
 
 // ------------------------------------------------------------------ errors
 void set_error(const char* fmt, ...);
+void count_launch();
 int fail(int code, const char* fmt, ...);          // set_error + return code
 
 #define RAGRT_CUDA_TRY(call)                                                              \
@@ -21,8 +22,10 @@ int fail(int code, const char* fmt, ...);          // set_error + return code
                                  cudaGetErrorString(e_));                                 \
     } while (0)
 
+// every kernel launch of the library is followed by this check, which also counts it
 #define RAGRT_LAUNCH_CHECK()                                                              \
     do {                                                                                  \
+        ::ragrt::count_launch();                                                          \
         cudaError_t e_ = cudaGetLastError();                                              \
         if (e_ != cudaSuccess)                                                            \
             return ::ragrt::fail(RAGRT_ERR_CUDA, "%s:%d kernel launch: %s", __FILE__,       \

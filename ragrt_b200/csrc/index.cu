@@ -7,6 +7,7 @@
 //   boff      per centroid and pid range, the first posting with pid >= range start
 //             (postings of a centroid are sorted by pid), so a Stage-3 tile reads only
 //             the sub-list that falls in its pid range.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -32,6 +33,9 @@ int fail(int code, const char* fmt, ...) {
     va_end(ap);
     return code;
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int num_sms() {
     int dev = 0, n = 148;
@@ -71,7 +75,6 @@ enum : int {
     kBadEids = 1 << 2,       // a centroid's chunk ids are not 0..k-1
     kBadOffsets = 1 << 3,    // block sums disagree with the lengths
     kBadPids = 1 << 4,       // a pid >= N or pids of a centroid not sorted
-    kBadLen = 1 << 5,        // an empty list
 };
 
 __global__ void k_list_offsets(const int64_t* __restrict__ bsums, const uint16_t* __restrict__ lengths,
@@ -98,7 +101,6 @@ __global__ void k_check_lists(const int64_t* __restrict__ off, const uint16_t* _
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= num_lists) return;
     if (off[i + 1] - off[i] != (int64_t)lengths[i]) atomicOr(flags, kBadOffsets);
-    if (lengths[i] == 0) atomicOr(flags, kBadLen);
     if (i == num_lists - 1 && off[num_lists] != num_postings) atomicOr(flags, kBadOffsets);
 }
 
@@ -253,12 +255,11 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
     if (h_flags) {
         cudaFree(flags);
         return cleanup(fail(RAGRT_ERR_INDEX,
-                            "not a valid plain-IVF index (flags 0x%x:%s%s%s%s%s)", h_flags,
+                            "not a valid plain-IVF index (flags 0x%x:%s%s%s%s)", h_flags,
                             (h_flags & kBadRow0) ? " row_ptrs row 0 malformed;" : "",
                             (h_flags & kBadRows) ? " subspace rows 1-31 not empty (weft needs a plain-IVF index);" : "",
                             (h_flags & kBadEids) ? " chunk ids of a centroid are not 0..k-1;" : "",
-                            (h_flags & kBadOffsets) ? " block sums disagree with lengths / num_postings;" : "",
-                            (h_flags & kBadLen) ? " empty posting list;" : ""));
+                            (h_flags & kBadOffsets) ? " block sums disagree with lengths / num_postings;" : ""));
     }
     k_check_pids<<<(unsigned)ceil_div((int64_t)NC * 32, T), T, 0, stream>>>(d.csr_packed_24, ix->cstart, ix->clists,
                                                                           d.csr_row_ptrs, ix->list_off, NC,
@@ -305,4 +306,5 @@ extern "C" int ragrt_index_stats(ragrt_index* ix, uint64_t* out, int32_t reset) 
 }
 
 extern "C" const char* ragrt_last_error(void) { return ragrt::g_err; }
+extern "C" uint64_t ragrt_launch_count(void) { return ragrt::g_launches.load(); }
 extern "C" const char* ragrt_version(void) { return "ragrt_b200 0.1.0 (sm_100a)"; }

@@ -245,6 +245,25 @@ class WeftIndex:
                                                RERANK_MODES[rerank], _ptr(ids), _ptr(sc), _stream()))
         return ids, sc
 
+    def search_profiled(self, Q, events, nc=32, K=4096, k_top=10, ntok=None, masks=None, rerank="tc",
+                        n_eids=None, out=None):
+        """search() recording 5 torch.cuda.Event objects at the stage boundaries (no sync)."""
+        Q = _c(Q, torch.float16)
+        B = Q.shape[0]
+        ids, sc = out if out is not None else (torch.empty(B, k_top, dtype=torch.int32, device=Q.device),
+                                               torch.empty(B, k_top, dtype=torch.float32, device=Q.device))
+        for e in events:
+            if not e.cuda_event:
+                e.record()                       # torch creates the event lazily
+        arr = (C.c_void_p * 5)(*[C.c_void_p(e.cuda_event) for e in events])
+        nt = _c(ntok, torch.int32) if ntok is not None else None
+        mk = _c(masks, torch.int32) if masks is not None else None
+        ne = self.E if n_eids is None else min(int(n_eids), self.E)
+        _lib.check(_lib.lib().ragrt_weft_search_profiled(self.handle, _ptr(Q), _ptr(nt), B, nc, ne, _ptr(mk), K,
+                                                        k_top, RERANK_MODES[rerank], _ptr(ids), _ptr(sc), arr,
+                                                        _stream()))
+        return ids, sc
+
     def stats(self, reset=False):
         buf = (C.c_uint64 * _lib.NUM_STATS)()
         _lib.check(_lib.lib().ragrt_index_stats(self.handle, buf, int(bool(reset))))
