@@ -180,6 +180,13 @@ int ragrt_index_stats(ragrt_index* index, uint64_t* out, int32_t reset);
 /* Message of the last failing call on this thread ("" if none). */
 const char* ragrt_last_error(void);
 
+/*
+ * Device-side failure status of the current device: 1 if a kernel gave up a bounded wait
+ * (a tensor-core pipeline stage that never completed) since the last reset, else 0 (<0 on
+ * error).  Synchronises with the device's error flag.  reset != 0 clears it.
+ */
+int ragrt_device_error(int32_t reset);
+
 /* Number of kernels this library has launched in the process (all entry points). */
 uint64_t ragrt_launch_count(void);
 

@@ -64,7 +64,7 @@ class _Csr(C.Structure):
 class _Docs(C.Structure):
     _fields_ = [("doc_offsets", C.c_void_p), ("doc_lens", C.c_void_p), ("codes", C.c_void_p),
                 ("residuals", C.c_void_p), ("centroids", C.c_void_p), ("bucket_weights", C.c_void_p),
-                ("rbm", C.c_void_p), ("decomp", C.c_void_p)]
+                ("rbm", C.c_void_p), ("decomp", C.c_void_p), ("num_passages", C.c_int)]
 
 
 def _p(a):
@@ -109,7 +109,7 @@ class Index:
                         _p(self.block_sums), _p(self.lengths), _p(self.packed), len(self.lengths),
                         self.N, self.NC, _p(self.preds))
         self.docs = _Docs(_p(self.doc_offsets), _p(self.doc_lens), _p(self.codes), _p(self.residuals),
-                          _p(self.centroids), _p(self.bw), _p(self.rbm), _p(self.decomp))
+                          _p(self.centroids), _p(self.bw), _p(self.rbm), _p(self.decomp), self.N)
 
 
 def rn16_dot(q, c):

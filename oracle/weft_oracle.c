@@ -307,6 +307,7 @@ typedef struct {
     const uint16_t* bucket_weights; /* [4] fp16 */
     const uint8_t* rbm;          /* [256] */
     const uint8_t* decomp;       /* [256, 4] */
+    int num_passages;            /* N: pids outside [0, N) score -inf */
 } oracle_docs;
 
 /* RN fp16 addition of two fp16 values (the kernels' __hadd). */
@@ -329,7 +330,7 @@ static uint16_t hadd_rn(uint16_t a, uint16_t b) {
 
 /* score of one candidate; Q [32,128] fp16 */
 static float tile_maxsim_one(const oracle_docs* D, const uint16_t* Q, int pid) {
-    if (pid < 0) return -INFINITY;
+    if (pid < 0 || pid >= D->num_passages) return -INFINITY;
     int64_t start = D->doc_offsets[pid];
     int L = D->doc_lens[pid];
     double runmax[32];

@@ -47,6 +47,7 @@ _SIGS = {
     "ragrt_last_error": (C.c_char_p, []),
     "ragrt_version": (C.c_char_p, []),
     "ragrt_launch_count": (C.c_uint64, []),
+    "ragrt_device_error": (I32, [I32]),
 }
 
 _lib = None

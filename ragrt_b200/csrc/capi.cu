@@ -28,12 +28,18 @@ struct Carve {
 };
 }  // namespace
 
+static size_t s2_ws_bytes(int B, int NC, int nc) {
+    const int kk = std::min(nc + 1, NC);
+    return std::max(s2_partial_bytes(B, kRows, NC, nc, 1),
+                    s2_tc_supported(kk, (int64_t)B * kRows) ? s2_tc_partial_bytes(B, kRows, NC, kk) : 0);
+}
+
 size_t weft_search_bytes(const ragrt_index* ix, int B, int nc, int K) {
     const int NC = ix->d.num_centroids;
     Carve c{nullptr};
     c.take<int32_t>((size_t)B * kRows * nc);       // topc
     c.take<float>((size_t)B * kRows * nc);         // scores
-    c.take<uint64_t>(s2_partial_bytes(B, kRows, NC, nc, 1) / sizeof(uint64_t) + 1);
+    c.take<uint64_t>(s2_ws_bytes(B, NC, nc) / sizeof(uint64_t) + 1);
     c.take<int32_t>((size_t)B * K);                // candidate pids
     c.take<float>((size_t)B * K);                  // candidate sums
     c.take<float>((size_t)B * K);                  // stage-4 scores
@@ -69,7 +75,7 @@ static int weft_search_impl(ragrt_index* ix, const void* d_Q, const int32_t* d_n
     Carve c{(char*)ix->ws.base};
     int32_t* topc = c.take<int32_t>((size_t)B * kRows * nc);
     float* scores = c.take<float>((size_t)B * kRows * nc);
-    uint64_t* partial = c.take<uint64_t>(s2_partial_bytes(B, kRows, NC, nc, 1) / sizeof(uint64_t) + 1);
+    uint64_t* partial = c.take<uint64_t>(s2_ws_bytes(B, NC, nc) / sizeof(uint64_t) + 1);
     int32_t* cand = c.take<int32_t>((size_t)B * K);
     float* csum = c.take<float>((size_t)B * K);
     float* fsc = c.take<float>((size_t)B * K);
@@ -78,8 +84,16 @@ static int weft_search_impl(ragrt_index* ix, const void* d_Q, const int32_t* d_n
     char* s3ws = c.take<char>(s3b);
 
     if ((rc = mark(0))) return rc;
-    rc = s2_run((const __half*)d_Q, d_ntok, B, kRows, (const __half*)ix->d.centroids, NC, nc, 1, topc, scores,
-                nullptr, nullptr, partial, stream);
+    const int kk = std::min(nc + 1, NC);
+    if (s2_tc_supported(kk, (int64_t)B * kRows)) {
+        int* err = device_error_flag();
+        if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
+        rc = s2_tc_run((const __half*)d_Q, d_ntok, B, kRows, (const __half*)ix->d.centroids, NC, ix->cnorm, ix->cnmax,
+                       nc, 1, topc, scores, nullptr, partial, err, stream);
+    } else {
+        rc = s2_run((const __half*)d_Q, d_ntok, B, kRows, (const __half*)ix->d.centroids, NC, nc, 1, topc, scores,
+                    nullptr, nullptr, partial, stream);
+    }
     if (rc || (rc = mark(1))) return rc;
     rc = s3_run(ix, topc, scores, 0, d_ntok, B, kRows, nc, std::min(n_eids, ix->d.num_eids), d_masks, K, cand, csum,
                 nullptr, s3ws, s3b, stream);

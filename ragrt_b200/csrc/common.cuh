@@ -99,5 +99,8 @@ __device__ __forceinline__ int32_t load_pid24(const uint8_t* __restrict__ p, int
 }
 
 int num_sms();
+// Per-device error flag that kernels raise (bounded waits that gave up); read and cleared
+// by ragrt_device_error().  Returns nullptr if it cannot be allocated.
+int* device_error_flag();
 
 }  // namespace ragrt

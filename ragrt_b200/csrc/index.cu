@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "index.cuh"
+#include "s2_common.cuh"
 
 namespace ragrt {
 
@@ -36,6 +37,19 @@ int fail(int code, const char* fmt, ...) {
 
 static std::atomic<unsigned long long> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int* device_error_flag() {
+    static int* flags[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!flags[dev]) {
+        int* f = nullptr;
+        if (cudaMalloc(&f, sizeof(int)) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+        cudaMemset(f, 0, sizeof(int));
+        flags[dev] = f;
+    }
+    return flags[dev];
+}
 
 int num_sms() {
     int dev = 0, n = 148;
@@ -164,18 +178,6 @@ __global__ void k_range_offsets(const uint8_t* __restrict__ packed, const int64_
     boff[i] = (uint32_t)lo;
 }
 
-__global__ void k_centroid_norms(const __half* __restrict__ C, int NC, float* __restrict__ out) {
-    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= NC) return;
-    double s = 0.0;
-    for (int k = lane; k < kDim; k += 32) {
-        double v = (double)__half2float(C[(int64_t)warp * kDim + k]);
-        s += v * v;
-    }
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-    if (lane == 0) out[warp] = __double2float_ru(sqrt(s) * (1.0 + 1e-6));
-}
-
 }  // namespace ragrt
 
 using namespace ragrt;
@@ -230,6 +232,7 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
     TRY_ALLOC(ix->clists, sizeof(int32_t) * NC);
     TRY_ALLOC(ix->boff, sizeof(uint32_t) * (size_t)NC * (R + 1));
     TRY_ALLOC(ix->cnorm, sizeof(float) * NC);
+    TRY_ALLOC(ix->cnmax, sizeof(float));
     TRY_ALLOC(ix->stats, sizeof(unsigned long long) * RAGRT_NUM_STATS);
 #undef TRY_ALLOC
     cudaMemsetAsync(flags, 0, sizeof(int), stream);
@@ -266,8 +269,10 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
                                                                           d.num_passages, flags);
     k_range_offsets<<<(unsigned)ceil_div((int64_t)NC * (R + 1), T), T, 0, stream>>>(
         d.csr_packed_24, ix->cstart, ix->clists, d.csr_row_ptrs, ix->list_off, NC, R, ws, ix->boff);
-    k_centroid_norms<<<(unsigned)ceil_div((int64_t)NC * 32, T), T, 0, stream>>>((const __half*)d.centroids, NC,
-                                                                               ix->cnorm);
+    if (s2_norms_launch((const __half*)d.centroids, NC, ix->cnorm, ix->cnmax, stream) != RAGRT_OK) {
+        cudaFree(flags);
+        return cleanup(RAGRT_ERR_CUDA);
+    }
     e = cudaMemcpyAsync(&h_flags, flags, sizeof(int), cudaMemcpyDeviceToHost, stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     cudaFree(flags);
@@ -286,6 +291,7 @@ extern "C" int ragrt_index_destroy(ragrt_index* ix) {
     cudaFree(ix->clists);
     cudaFree(ix->boff);
     cudaFree(ix->cnorm);
+    cudaFree(ix->cnmax);
     cudaFree(ix->stats);
     cudaFree(ix->ws.base);
     delete ix;
@@ -306,5 +312,14 @@ extern "C" int ragrt_index_stats(ragrt_index* ix, uint64_t* out, int32_t reset) 
 }
 
 extern "C" const char* ragrt_last_error(void) { return ragrt::g_err; }
+extern "C" int ragrt_device_error(int32_t reset) {
+    int* f = ragrt::device_error_flag();
+    if (!f) return ragrt::fail(RAGRT_ERR_CUDA, "device error flag unavailable");
+    int h = 0;
+    RAGRT_CUDA_TRY(cudaMemcpy(&h, f, sizeof(int), cudaMemcpyDeviceToHost));
+    if (reset && h) RAGRT_CUDA_TRY(cudaMemset(f, 0, sizeof(int)));
+    return h;
+}
+
 extern "C" uint64_t ragrt_launch_count(void) { return ragrt::g_launches.load(); }
 extern "C" const char* ragrt_version(void) { return "ragrt_b200 0.1.0 (sm_100a)"; }

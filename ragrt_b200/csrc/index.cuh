@@ -21,6 +21,7 @@ struct ragrt_index {
     int32_t* clists = nullptr;     // [NC] number of lists (chunks) of centroid c
     uint32_t* boff = nullptr;      // [NC, R + 1] first posting (relative to cstart) with pid >= r*W
     float* cnorm = nullptr;        // [NC] |c|_2 of each centroid, rounded up
+    float* cnmax = nullptr;        // [1] max over cnorm
 
     ragrt_workspace ws;
     unsigned long long* stats = nullptr;   // [RAGRT_NUM_STATS]

@@ -1,0 +1,539 @@
+// s2_tc.cu -- Stage 2 on the tensor cores: fp16 query-token x centroid scores with tcgen05
+// (accumulators in tensor memory, operands staged by TMA) and a fused, exact top-(nc+1)
+// epilogue.  The reference computes Q @ C^T with a cuBLAS fp16 GEMM and torch.topk per
+// query (src/weft_prep.py:32-47); the full [32, NC] score matrix is never materialised here.
+//
+// CTA = 128 query rows (4 queries of 32 tokens) x one slice of the centroids.
+//   warp 0 : TMA producer -- the 128 x 128 query tile once, then 128-centroid x 128-dim
+//            tiles of C through a ring of shared-memory stages (128-byte swizzle, K-major)
+//   warp 1 : MMA issuer -- per tile 8 x tcgen05.mma (M=128, N=128, K=16) into one of four
+//            tensor-memory accumulators (4 x 128 columns = all 512)
+//   warps 2-5 (epilogue, one per tensor-memory lane quadrant, thread = query row): drain
+//            the accumulator with tcgen05.ld, release it, then maintain the row's candidate
+//            superset.  Each fp32 accumulation brackets the exact fp16 score:
+//            lo = RN16(acc - eps) <= RN16(exact) <= hi = RN16(acc + eps) (s2_common.cuh).
+//            The list is ordered by the lower-bound key (lo, centroid asc); T = its kk-th key.
+//            A value enters if its upper-bound key (hi, centroid) beats T; entries below the
+//            kk-th place survive only while their upper bound still beats T.  The exact top-kk
+//            is a subset of this superset, so no value is resolved exactly here: a 32-value
+//            chunk whose max is below the row's admission bound is skipped outright.
+// Each CTA writes its rows' supersets (KX = kk + 31 keys, bit 0 = "lo != hi") to
+// partial[query][slice][token][KX]; s2_merge_tc takes the global superset across slices,
+// resolves only its ambiguous members with an exact fp64 dot product and selects the
+// exact top-kk.  All waits are bounded; a timeout raises an error flag and every role exits.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "s2_common.cuh"
+#include "tc.cuh"
+
+namespace ragrt {
+
+constexpr int kQM = 128;                       // query rows per CTA
+constexpr int kCN = 128;                       // centroids per tile
+constexpr int kAccBufs = 4;                    // tensor-memory accumulators (128 columns each)
+constexpr int kS2TcThreads = 192;
+constexpr uint32_t kTileBytes = kCN * 256;     // 32 KB: two 16 KB K-atoms
+constexpr uint32_t kQTileBytes = kQM * 256;    // 32 KB
+constexpr uint32_t kS2WaitLimit = 1u << 24;
+
+struct S2TcParams {
+    const __half* Q;
+    const __half* C;
+    const float* cnorm;
+    const float* cnmax;          // device scalar: max centroid norm
+    const int32_t* ntok;
+    uint64_t* partial;
+    unsigned long long* gthr;    // [rows_total] best k-th lower-bound key of the row over all slices
+    int* err;
+    int rows_total, rows, NC, kk, tiles_total, tiles_per_slice, nslices, stages;
+};
+
+constexpr int kExtra = 31;                     // superset slots beyond kk
+
+// superset key: (ord16(lo) << 32) | ((0x7FFFFFFF - id) << 1) | ambiguous;  orders by (lo desc, id asc)
+__device__ __forceinline__ uint64_t sk_make(uint16_t lo, uint32_t id, uint32_t amb) {
+    if (lo == 0x8000u) lo = 0;
+    return ((uint64_t)ord16(lo) << 32) | ((uint64_t)(0x7FFFFFFFu - id) << 1) | (uint64_t)amb;
+}
+__device__ __forceinline__ uint32_t sk_id(uint64_t k) { return 0x7FFFFFFFu - ((uint32_t)k >> 1); }
+__device__ __forceinline__ uint16_t f16_next(uint16_t h) {
+    if (h == 0x8000u || h == 0) return 1;
+    return (h & 0x8000u) ? (uint16_t)(h - 1) : (uint16_t)(h + 1);
+}
+// key of the upper bound (flag cleared): hi = next(lo) for an ambiguous entry
+__device__ __forceinline__ uint64_t sk_hi(uint64_t k) {
+    if (!(k & 1)) return k;
+    const uint16_t lo = unord16((uint32_t)(k >> 32));
+    return sk_make(f16_next(lo), sk_id(k), 0);
+}
+
+__device__ __forceinline__ float f16_next_mid(uint16_t h) {
+    // midpoint between fp16 h and the next larger fp16 value (h finite)
+    uint16_t n;
+    if (h == 0x8000u || h == 0) n = 1;
+    else if (h & 0x8000u) n = (uint16_t)(h - 1);
+    else n = (uint16_t)(h + 1);
+    const float a = __half2float(__ushort_as_half(h)), b = __half2float(__ushort_as_half(n));
+    return 0.5f * (a + b);
+}
+
+__global__ void __launch_bounds__(kS2TcThreads, 1)
+s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmC, S2TcParams p) {
+    extern __shared__ uint8_t s2_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)s2_raw + 1023) & ~(uintptr_t)1023);
+    const int S = p.stages, kk = p.kk;
+    uint8_t* sA = sm;
+    uint8_t* sB = sm + kQTileBytes;
+    uint64_t* lists = reinterpret_cast<uint64_t*>(sB + (size_t)S * kTileBytes);    // [kk + kExtra][128]
+    float* scratch = reinterpret_cast<float*>(lists + (size_t)(kk + kExtra) * kQM); // [32][128]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + 32 * kQM);
+    uint64_t* fullA = bars;
+    uint64_t* full = bars + 1;
+    uint64_t* empty = full + S;
+    uint64_t* accf = empty + S;
+    uint64_t* acce = accf + kAccBufs;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + kAccBufs);
+    volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slice = blockIdx.x, rb = blockIdx.y;
+    const int t0 = slice * p.tiles_per_slice;
+    const int ntiles = min(p.tiles_total, t0 + p.tiles_per_slice) - t0;
+
+    for (int i = threadIdx.x; i < (kk + kExtra) * kQM; i += blockDim.x) lists[i] = 0ull;
+    if (threadIdx.x == 0) {
+        tc::mbar_init(fullA, 1);
+        for (int s = 0; s < S; ++s) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
+        for (int b = 0; b < kAccBufs; ++b) { tc::mbar_init(accf + b, 1); tc::mbar_init(acce + b, 4); }
+        *abort = 0;
+        tc::mbar_fence_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tslot, kAccBufs * kCN);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0 && ntiles > 0) {
+            tc::mbar_arrive_expect_tx(fullA, kQTileBytes);
+            tc::tma_load_2d(sA, &tmQ, 0, rb * kQM, fullA);
+            tc::tma_load_2d(sA + kQTileBytes / 2, &tmQ, 64, rb * kQM, fullA);
+            for (int i = 0; i < ntiles; ++i) {
+                const int s = i % S;
+                if (i >= S && !tc::mbar_wait_or_abort(empty + s, ((i / S) - 1) & 1, abort, kS2WaitLimit)) break;
+                uint8_t* dst = sB + (size_t)s * kTileBytes;
+                tc::mbar_arrive_expect_tx(full + s, kTileBytes);
+                tc::tma_load_2d(dst, &tmC, 0, (t0 + i) * kCN, full + s);
+                tc::tma_load_2d(dst + kTileBytes / 2, &tmC, 64, (t0 + i) * kCN, full + s);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0 && ntiles > 0) {
+            constexpr uint32_t idesc = tc::idesc_f16_f32(kQM, kCN);
+            const uint32_t aBase = tc::smem_u32(sA);
+            bool ok = tc::mbar_wait_or_abort(fullA, 0, abort, kS2WaitLimit);
+            for (int i = 0; ok && i < ntiles; ++i) {
+                const int s = i % S, b = i % kAccBufs;
+                if (!tc::mbar_wait_or_abort(full + s, (i / S) & 1, abort, kS2WaitLimit)) break;
+                if (i >= kAccBufs && !tc::mbar_wait_or_abort(acce + b, ((i / kAccBufs) - 1) & 1, abort, kS2WaitLimit))
+                    break;
+                tc::fence_after();
+                const uint32_t bBase = tc::smem_u32(sB + (size_t)s * kTileBytes);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint32_t koffA = (uint32_t)((k >> 2) * (kQTileBytes / 2) + (k & 3) * 32);
+                    const uint32_t koffB = (uint32_t)((k >> 2) * (kTileBytes / 2) + (k & 3) * 32);
+                    tc::mma_ss(tbase + (uint32_t)(b * kCN), tc::sw128_kmajor_desc(aBase + koffA),
+                               tc::sw128_kmajor_desc(bBase + koffB), idesc, k > 0);
+                }
+                tc::mma_commit(empty + s);
+                tc::mma_commit(accf + b);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (thread = row)
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int grow = rb * kQM + r;
+        const int qb = grow / p.rows, tok = grow % p.rows;
+        const bool valid = grow < p.rows_total && tok < (p.ntok ? min(p.ntok[qb], p.rows) : p.rows);
+        const __half* qrow = p.Q + (int64_t)(valid ? grow : 0) * kDim;
+        float qn = 0.f;
+        if (valid) {
+            for (int k = 0; k < kDim; k += 8) {
+                uint4 u = *reinterpret_cast<const uint4*>(qrow + k);
+                const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float2 f = __half22float2(h[j]);
+                    qn = fmaf(f.x, f.x, fmaf(f.y, f.y, qn));
+                }
+            }
+            qn = __fsqrt_ru(qn) * (1.0f + 1e-6f);
+        }
+        const float eps_max = qn * (*p.cnmax) * kEpsTc;
+        const int KX = kk + kExtra;
+        int cnt = 0;
+        uint64_t T = 0;                       // kk-th lower-bound key (flag cleared) once cnt >= kk
+        uint64_t Te = 0;                      // admission key: max(T, best T of this row's other slices)
+        float thr_lo = -INFINITY;             // acc below this cannot produce an upper bound > Te
+        unsigned long long* gT = p.gthr + (valid ? grow : 0);
+        auto raise = [&](uint64_t k) {        // Te only grows; publish it and move the chunk filter
+            if (k <= Te) return;
+            Te = k;
+            const float mid = f16_next_mid(unord16((uint32_t)(Te >> 32)));
+            thr_lo = mid - (eps_max + fabsf(mid) * 2.4e-7f + 1e-30f);
+        };
+        for (int i = 0; i < ntiles; ++i) {
+            const int b = i % kAccBufs;
+            const bool ok = tc::mbar_wait_or_abort(accf + b, (i / kAccBufs) & 1, abort, kS2WaitLimit);
+            if (!__all_sync(0xFFFFFFFFu, ok)) break;          // warp-uniform: tcgen05.ld is warp-collective
+            tc::fence_after();
+            uint32_t v[4][32];
+            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kCN);
+            tc::ld32x32(taddr, v[0]);
+            tc::ld32x32(taddr + 32, v[1]);
+            tc::ld32x32(taddr + 64, v[2]);
+            tc::ld32x32(taddr + 96, v[3]);
+            tc::wait_ld();
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(acce + b);
+            if (!valid) continue;
+            raise(*reinterpret_cast<volatile unsigned long long*>(gT));   // other slices' progress
+            const int c0 = (t0 + i) * kCN;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                float m16[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) m16[j] = fmaxf(__uint_as_float(v[ch][j]), __uint_as_float(v[ch][j + 16]));
+#pragma unroll
+                for (int w2 = 8; w2 >= 1; w2 >>= 1)
+#pragma unroll
+                    for (int j = 0; j < w2; ++j) m16[j] = fmaxf(m16[j], m16[j + w2]);
+                const float mx = m16[0];
+                if (!(mx >= thr_lo)) continue;
+                uint32_t cand = 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    scratch[j * kQM + r] = __uint_as_float(v[ch][j]);
+                    cand |= (__uint_as_float(v[ch][j]) >= thr_lo) ? (1u << j) : 0u;
+                }
+                while (cand) {
+                    const int j = __ffs(cand) - 1;
+                    cand &= cand - 1;
+                    const int c = c0 + ch * 32 + j;
+                    const float acc = scratch[j * kQM + r];
+                    if (c >= p.NC || !(acc >= thr_lo)) continue;
+                    const float eps = fmaf(fabsf(acc), 1.2e-7f, qn * p.cnorm[c] * kEpsTc);
+                    const uint16_t hi = __half_as_ushort(__float2half_rn(acc + eps));
+                    if (sk_make(hi, (uint32_t)c, 0) <= Te) continue;
+                    uint16_t lo = __half_as_ushort(__float2half_rn(acc - eps));
+                    uint32_t amb = lo != hi;
+                    if (amb && f16_next(lo == 0x8000u ? 0 : lo) != (hi == 0x8000u ? 0 : hi)) {
+                        // the bracket spans more than one fp16 step (tiny scores): resolve now
+                        lo = s2_exact(qrow, p.C + (int64_t)c * kDim);
+                        amb = 0;
+                        if (sk_make(lo, (uint32_t)c, 0) <= Te) continue;
+                    }
+                    while (cnt == KX) {
+                        // full (rare): resolve the ambiguous tail entries exactly and re-rank.  Each
+                        // pass resolves at least one entry; once the tail holds only exact keys they
+                        // all rank below the kk-th entry, fall under T and are trimmed.
+                        for (int e = kk; e < cnt; ++e) {
+                            const uint64_t k = lists[e * kQM + r];
+                            if (k & 1) {
+                                const uint32_t id = sk_id(k);
+                                lists[e * kQM + r] = sk_make(s2_exact(qrow, p.C + (int64_t)id * kDim), id, 0);
+                            }
+                        }
+                        for (int e = 1; e < cnt; ++e) {
+                            const uint64_t k = lists[e * kQM + r];
+                            int q = e;
+                            while (q > 0 && lists[(q - 1) * kQM + r] < k) {
+                                lists[q * kQM + r] = lists[(q - 1) * kQM + r];
+                                --q;
+                            }
+                            lists[q * kQM + r] = k;
+                        }
+                        T = lists[(kk - 1) * kQM + r] & ~1ull;
+                        int w = kk;
+                        for (int e = kk; e < cnt; ++e) {
+                            const uint64_t k = lists[e * kQM + r];
+                            if (sk_hi(k) > T) lists[w++ * kQM + r] = k;
+                        }
+                        cnt = w;
+                    }
+                    if (sk_make(hi, (uint32_t)c, 0) <= Te || (cnt >= kk && sk_make(hi, (uint32_t)c, 0) <= T)) continue;
+                    const uint64_t key = sk_make(lo, (uint32_t)c, amb);
+                    int pos = cnt;
+                    while (pos > 0 && lists[(pos - 1) * kQM + r] < key) {
+                        lists[pos * kQM + r] = lists[(pos - 1) * kQM + r];
+                        --pos;
+                    }
+                    lists[pos * kQM + r] = key;
+                    ++cnt;
+                    if (cnt >= kk) {
+                        T = lists[(kk - 1) * kQM + r] & ~1ull;
+                        int w = kk;                   // keep tail entries whose upper bound beats T
+                        for (int e = kk; e < cnt; ++e) {
+                            const uint64_t k = lists[e * kQM + r];
+                            if (sk_hi(k) > T) lists[w++ * kQM + r] = k;
+                        }
+                        cnt = w;
+                        if (T > Te) {
+                            atomicMax(gT, (unsigned long long)T);
+                            raise(T);
+                        }
+                    }
+                }
+            }
+        }
+        if (valid) {
+            uint64_t* out = p.partial + (((int64_t)qb * p.nslices + slice) * p.rows + tok) * (kk + kExtra);
+            for (int j = 0; j < kk + kExtra; ++j) out[j] = j < cnt ? lists[j * kQM + r] : 0ull;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && *abort) atomicExch(p.err, 1);
+    if (warp == 1) {
+        tc::fence_after();
+        tc::tmem_dealloc(tbase, kAccBufs * kCN);
+    }
+}
+
+// ------------------------------------------------------------------ merge of the slice supersets
+// Warp per (query, row).  T = kk-th best lower-bound key over all slices (a tournament over
+// the slices' sorted lists, lane = slice); members of the global superset are the entries
+// whose upper bound beats T; the ambiguous ones get an exact fp64 dot product (warp-wide, 4
+// dims per lane; every partial sum is a multiple of 2^-48 below 2^5, hence exact); the exact
+// top-kk is then taken by (value desc, centroid asc).
+__global__ void s2_merge_tc(const uint64_t* __restrict__ partial, int nslices, int KX, const int32_t* __restrict__ ntok,
+                            int B, int rows, int kk, int nc, int impute, const __half* __restrict__ Q,
+                            const __half* __restrict__ C, int32_t* __restrict__ topc, float* __restrict__ scores,
+                            float* __restrict__ m) {
+    extern __shared__ uint64_t s_ent[];
+    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int E = nslices * KX;
+    uint64_t* ent = s_ent + (size_t)wib * (E + kk);
+    uint64_t* outk = ent + E;
+    const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + wib;
+    if (gw >= (int64_t)B * rows) return;
+    const int b = (int)(gw / rows), t = (int)(gw % rows);
+    const int ncol = min(nc, kk);
+    const bool imputed = impute && kk > nc;
+    const int nt = ntok ? min(ntok[b], rows) : rows;
+    int32_t* tc_ = topc + ((int64_t)b * rows + t) * ncol;
+    float* sc = scores + ((int64_t)b * rows + t) * ncol;
+    if (t >= nt) {
+        for (int j = lane; j < ncol; j += 32) { tc_[j] = -1; sc[j] = 0.f; }
+        if (m && lane == 0) m[(int64_t)b * rows + t] = 0.f;
+        return;
+    }
+    for (int i = lane; i < E; i += 32) {
+        const int s = i / KX, j = i % KX;
+        ent[i] = partial[(((int64_t)b * nslices + s) * rows + t) * KX + j];
+    }
+    __syncwarp();
+    // 1. T: the kk-th lower-bound key over all slices
+    uint64_t T = 0;
+    {
+        int pos = 0;
+        for (int j = 0; j < kk; ++j) {
+            const uint64_t h = (lane < nslices && pos < KX) ? ent[lane * KX + pos] : 0ull;
+            uint64_t mx = h;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const uint64_t x = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+                mx = x > mx ? x : mx;
+            }
+            const unsigned win = __ballot_sync(0xFFFFFFFFu, h == mx && mx != 0);
+            if (win && lane == __ffs(win) - 1) ++pos;
+            T = mx & ~1ull;
+        }
+    }
+    // 2. keep the global superset; resolve its ambiguous members exactly
+    const __half* qrow = Q + ((int64_t)b * rows + t) * kDim;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+        const int e = e0 + lane;
+        uint64_t k = e < E ? ent[e] : 0ull;
+        bool member = k != 0 && ((k & ~1ull) >= T || sk_hi(k) > T);
+        if (!member && e < E) ent[e] = 0ull;
+        unsigned need = __ballot_sync(0xFFFFFFFFu, member && (k & 1));
+        while (need) {
+            const int src = __ffs(need) - 1;
+            need &= need - 1;
+            const uint64_t ks = __shfl_sync(0xFFFFFFFFu, k, src);
+            const uint32_t id = sk_id(ks);
+            const uint2 qv = *reinterpret_cast<const uint2*>(qrow + 4 * lane);
+            const uint2 cv = *reinterpret_cast<const uint2*>(C + (int64_t)id * kDim + 4 * lane);
+            const __half* qh = reinterpret_cast<const __half*>(&qv);
+            const __half* ch = reinterpret_cast<const __half*>(&cv);
+            double d = 0.0;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) d = fma((double)__half2float(qh[u]), (double)__half2float(ch[u]), d);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
+            if (lane == src) {
+                uint16_t h = d2h_rn(d);
+                k = sk_make(h == 0x8000u ? 0 : h, id, 0);
+                ent[e] = k;
+            }
+        }
+    }
+    __syncwarp();
+    // 3. exact top-kk by (value desc, centroid asc)
+    for (int j = 0; j < kk; ++j) {
+        uint64_t best = 0;
+        int bi = -1;
+        for (int e = lane; e < E; e += 32) {
+            const uint64_t k = ent[e];
+            if (k > best) { best = k; bi = e; }
+        }
+        uint64_t mx = best;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const uint64_t x = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+            mx = x > mx ? x : mx;
+        }
+        const unsigned win = __ballot_sync(0xFFFFFFFFu, best == mx && mx != 0);
+        if (win && lane == __ffs(win) - 1) ent[bi] = 0ull;
+        if (lane == 0) outk[j] = mx;
+        __syncwarp();
+    }
+    __syncwarp();
+    float mt = 0.f;
+    if (imputed) mt = __half2float(__ushort_as_half(unord16((uint32_t)(outk[nc] >> 32))));
+    for (int j = lane; j < ncol; j += 32) {
+        const uint64_t k = outk[j];
+        tc_[j] = k ? (int32_t)sk_id(k) : -1;
+        const float v = __half2float(__ushort_as_half(unord16((uint32_t)(k >> 32))));
+        sc[j] = imputed ? __fsub_rn(v, mt) : v;
+    }
+    if (m && lane == 0) m[(int64_t)b * rows + t] = imputed ? mt : 0.f;
+}
+
+// max centroid norm (for the chunk filter's error bound) and, optionally, all norms
+__global__ void s2_centroid_norms(const __half* __restrict__ C, int NC, float* __restrict__ cn,
+                                  float* __restrict__ cnmax) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= NC) return;
+    float s = 0.f;
+    for (int k = lane; k < kDim; k += 32) {
+        const float v = __half2float(C[(int64_t)warp * kDim + k]);
+        s = fmaf(v, v, s);
+    }
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    if (lane == 0) {
+        const float n = __fsqrt_ru(s) * (1.0f + 1e-6f);
+        cn[warp] = n;
+        atomicMax(reinterpret_cast<unsigned int*>(cnmax), __float_as_uint(n));   // non-negative floats
+    }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)f;
+    }
+    return fn;
+}
+
+// 2-D fp16 tensor [rows, 128] with a [128 rows x 64 cols] box, 128-byte swizzle
+static int make_map(CUtensorMap* m, const void* base, int64_t rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(RAGRT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {(cuuint64_t)kDim, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kDim * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RAGRT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return RAGRT_OK;
+}
+
+static size_t s2_tc_smem(int kk, int stages) {
+    return 1024 + kQTileBytes + (size_t)stages * kTileBytes + (size_t)(kk + kExtra) * kQM * 8 + 32 * kQM * 4 +
+           8 * (1 + 2 * stages + 2 * kAccBufs) + 16;
+}
+
+bool s2_tc_supported(int kk, int64_t rows_total) {
+    return rows_total >= kQM && kk <= 64 && s2_tc_smem(kk, 2) <= 227 * 1024;
+}
+
+void s2_tc_plan(int B, int rows, int NC, int& nslices, int& tiles_per_slice) {
+    const int rbs = (int)ceil_div((int64_t)B * rows, kQM);
+    const int tiles = (int)ceil_div(NC, kCN);
+    const int sms = num_sms();
+    // one wave of CTAs: every extra slice re-pays the top-k warm-up of each row
+    const int best = (int)std::max<int64_t>(1, std::min<int64_t>({32, (int64_t)tiles, sms / std::max(1, rbs)}));
+    tiles_per_slice = (int)ceil_div(tiles, best);
+    nslices = (int)ceil_div(tiles, tiles_per_slice);
+}
+
+size_t s2_tc_partial_bytes(int B, int rows, int NC, int kk) {
+    int ns, tps;
+    s2_tc_plan(B, rows, NC, ns, tps);
+    return sizeof(uint64_t) * (size_t)B * ns * rows * (kk + kExtra) + sizeof(uint64_t) * (size_t)B * rows + 256;
+}
+
+int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __half* C, int NC, const float* cnorm,
+              const float* cnmax, int nc, int impute, int32_t* topc, float* scores, float* m, uint64_t* partial,
+              int* err, cudaStream_t stream) {
+    const int kk = std::min(nc + (impute ? 1 : 0), NC);
+    int nslices, tps;
+    s2_tc_plan(B, rows, NC, nslices, tps);
+    CUtensorMap tmQ, tmC;
+    int rc = make_map(&tmQ, Q, (int64_t)B * rows);
+    if (rc) return rc;
+    if ((rc = make_map(&tmC, C, NC))) return rc;
+    int stages = 4;
+    while (stages > 2 && s2_tc_smem(kk, stages) > 227 * 1024) --stages;
+    const size_t smem = s2_tc_smem(kk, stages);
+    unsigned long long* gthr = reinterpret_cast<unsigned long long*>(
+        partial + (size_t)B * nslices * rows * (kk + kExtra));
+    RAGRT_CUDA_TRY(cudaMemsetAsync(gthr, 0, sizeof(uint64_t) * (size_t)B * rows, stream));
+    S2TcParams p{Q, C, cnorm, cnmax, ntok, partial, gthr, err, B * rows, rows, NC, kk, (int)ceil_div(NC, kCN), tps,
+                 nslices, stages};
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid(nslices, (unsigned)ceil_div((int64_t)B * rows, kQM));
+    s2_tc<<<grid, kS2TcThreads, smem, stream>>>(tmQ, tmC, p);
+    RAGRT_LAUNCH_CHECK();
+    const int KX = kk + kExtra;
+    const int warps = 4;
+    const size_t msmem = sizeof(uint64_t) * warps * ((size_t)nslices * KX + kk);
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_merge_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
+    s2_merge_tc<<<(unsigned)ceil_div((int64_t)B * rows, warps), warps * 32, msmem, stream>>>(
+        partial, nslices, KX, ntok, B, rows, kk, nc, impute, Q, C, topc, scores, m);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}
+
+int s2_norms_launch(const __half* C, int NC, float* cn, float* cnmax, cudaStream_t stream) {
+    RAGRT_CUDA_TRY(cudaMemsetAsync(cnmax, 0, sizeof(float), stream));
+    s2_centroid_norms<<<(unsigned)ceil_div((int64_t)NC * 32, 256), 256, 0, stream>>>(C, NC, cn, cnmax);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}
+
+}  // namespace ragrt

@@ -166,7 +166,23 @@ extern "C" int ragrt_centroid_topk(const void* d_Q, const int32_t* d_ntok, int32
     cudaStream_t stream = (cudaStream_t)stream_;
     int rc = s2_check(d_Q, d_C, B, rows, NC, nc, d_topc, d_scores);
     if (rc) return rc;
+    const int kk = std::min(nc + (impute ? 1 : 0), NC);
     uint64_t* partial = nullptr;
+    if (!d_full16 && s2_tc_supported(kk, (int64_t)B * rows)) {
+        // tensor-core path: centroid norms for the exactness bound, then the fused GEMM + top-k
+        int* err = device_error_flag();
+        if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
+        float* norms = nullptr;
+        RAGRT_CUDA_TRY(cudaMallocAsync((void**)&norms, sizeof(float) * (NC + 1), stream));
+        RAGRT_CUDA_TRY(cudaMallocAsync((void**)&partial, s2_tc_partial_bytes(B, rows, NC, kk), stream));
+        rc = s2_norms_launch((const __half*)d_C, NC, norms, norms + NC, stream);
+        if (!rc)
+            rc = s2_tc_run((const __half*)d_Q, d_ntok, B, rows, (const __half*)d_C, NC, norms, norms + NC, nc, impute,
+                           d_topc, d_scores, d_m, partial, err, stream);
+        cudaFreeAsync(partial, stream);
+        cudaFreeAsync(norms, stream);
+        return rc;
+    }
     RAGRT_CUDA_TRY(cudaMallocAsync((void**)&partial, s2_partial_bytes(B, rows, NC, nc, impute), stream));
     rc = s2_run((const __half*)d_Q, d_ntok, B, rows, (const __half*)d_C, NC, nc, impute, d_topc, d_scores, d_m,
                 (__half*)d_full16, partial, stream);

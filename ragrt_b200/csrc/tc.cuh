@@ -140,3 +140,61 @@ __device__ __forceinline__ float warp_max_f32(float v) {
 
 }  // namespace tc
 }  // namespace ragrt
+
+namespace ragrt {
+namespace tc {
+
+// TMA: 2-D tiled bulk tensor load into shared memory, completion counted in bytes on `bar`.
+// x (innermost, elements) must keep x * element size a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait that also gives up as soon as another role raised `abort` (shared flag).
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* m, uint32_t parity, volatile int* abort, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait(m, parity)) return true;
+        if ((i & 63) == 63 && *abort) return false;
+    }
+    *abort = 1;
+    return false;
+}
+
+}  // namespace tc
+}  // namespace ragrt
+
+namespace ragrt {
+namespace tc {
+
+// Named barrier over `nthreads` threads with an OR / AND reduction of a predicate.
+__device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+        "barrier.cta.red.or.pred po, %2, %3, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)p), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ bool bar_red_and(int id, int nthreads, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+        "barrier.cta.red.and.pred po, %2, %3, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)p), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
+}  // namespace tc
+}  // namespace ragrt

@@ -1,0 +1,90 @@
+"""
+Per-stage benchmark of the `weft` kernels on seeded synthetic data (one GPU).
+
+    python -m ragrt_b200.stagebench --stage s2|s3|s4|all [--docs N] [--batch B] [--steps K]
+
+  s2   Stage 2 alone: B x 32 query tokens against 65,536 fp16 centroids, top-(nc+1).
+  s3   Stages 1-3 alone on Stage-2 output (posting aggregation + candidate selection).
+  s4   Stage 4 alone: 4,096 candidates per query drawn uniformly
+       without replacement from the corpus (seeded per query), fused 2-bit decompression
+       + TileMaxSim, batch B.
+Prints one JSON line per stage with the mean time per step (CUDA events on the launching
+stream, after warm-up) and the stage's algorithmic work.  Also the program that the ncu
+captures in profiles/ run.
+"""
+import argparse
+import json
+import sys
+import time
+
+import torch
+
+from . import synth, index_build
+from .weft import WeftIndex, centroid_topk
+
+
+def timed(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--stage", default="all", choices=("s2", "s3", "s4", "all"))
+    ap.add_argument("--docs", type=int, default=2_000_000)
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--nc", type=int, default=32)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--rerank", default="tc", choices=("tc", "simt"))
+    a = ap.parse_args()
+    dev = "cuda"
+    t0 = time.time()
+    centres, C = synth.make_centroids(num_centres=1024, subs=64, seed=0, device=dev)
+    Q = synth.make_queries(centres, a.batch, seed=1000).view(a.batch, 32, 128)
+    stages = ("s2", "s3", "s4") if a.stage == "all" else (a.stage,)
+    out = []
+    if "s2" in stages:
+        ms = timed(lambda: centroid_topk(Q, C, a.nc), a.steps, a.warmup)
+        flops = 2.0 * a.batch * 32 * C.shape[0] * 128
+        out.append({"stage": "s2", "ms": ms, "tflops": flops / ms / 1e9, "work_gflop": flops / 1e9})
+    if "s3" in stages or "s4" in stages:
+        corp = synth.make_corpus(a.docs, centres, C, seed=0, device=dev)
+        ix = index_build.plain_ivf_index(corp["codes"], corp["doclens"], C.shape[0])
+        wix = WeftIndex(ix["csr_row_ptrs"], ix["csr_col_eids"], ix["csr_block_sums"], ix["csr_lengths"],
+                        ix["csr_packed_24"], corp["doc_offsets"], corp["doclens"], corp["codes"], corp["residuals"],
+                        C, corp["bucket_weights"], corp["reversed_bit_map"], corp["decomp_table"], E=ix["E"])
+        print(f"corpus ready in {time.time() - t0:.1f} s", file=sys.stderr)
+        if "s3" in stages:
+            topc, sc, _, _ = centroid_topk(Q, C, a.nc)
+            wix.stats(reset=True)
+            ms = timed(lambda: wix.candidates(topc, sc, a.K), a.steps, a.warmup)
+            st = wix.stats()
+            n = a.steps + a.warmup
+            b = (3.0 * st["distinct_postings"] + 8.0 * st["touched"]) / n
+            out.append({"stage": "s3", "ms": ms, "gbs": b / ms / 1e6, "postings_per_query": st["postings"] / n / a.batch,
+                        "distinct_postings_per_query": st["distinct_postings"] / n / a.batch,
+                        "touched_per_query": st["touched"] / n / a.batch})
+        if "s4" in stages:
+            cand = synth.random_candidates(a.docs, a.batch, a.K, seed=0, device=dev)
+            mode = 1 if a.rerank == "tc" else 0
+            ms = timed(lambda: wix.tile_maxsim(Q, cand, mode=mode), a.steps, a.warmup)
+            toks = int(wix.doc_lens[cand.long()].sum())
+            b = 36.0 * toks + 16.0 * cand.numel()
+            out.append({"stage": "s4", "ms": ms, "gbs": b / ms / 1e6, "doc_tokens_per_s": toks / ms * 1e3,
+                        "tflops": 2.0 * 32 * 128 * toks / ms / 1e9, "doc_tokens": toks, "rerank": a.rerank})
+    for o in out:
+        print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in o.items()}), flush=True)
+
+
+if __name__ == "__main__":
+    main()

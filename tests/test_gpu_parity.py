@@ -199,3 +199,23 @@ def test_invalid_index_is_rejected():
     from tests.helpers import weft_index as mk
     with pytest.raises(RagrtError, match="not a valid plain-IVF index"):
         mk(bad, E)
+
+
+@pytest.mark.parametrize("nq,ntok_drop", [(8, 0), (5, 7)])
+def test_stage2_tensor_core_many_tiles(nq, ntok_drop):
+    """Stage 2 with several 128-row tiles and centroid slices (the tcgen05 path) is bit-exact."""
+    from ragrt_b200 import synth
+    from ragrt_b200.weft import centroid_topk
+    centres, C = synth.make_centroids(num_centres=256, subs=32, seed=9)        # 8,192 centroids
+    Q = synth.make_queries(centres, nq, seed=9)
+    ntok = torch.tensor([32 - (ntok_drop if b % 2 else 0) for b in range(nq)], dtype=torch.int32)
+    topc, sc, m, _ = centroid_topk(Q.cuda(), C.cuda(), 32, impute=True, ntok=ntok.cuda())
+    topc, sc, m = topc.cpu().numpy(), sc.cpu().numpy(), m.cpu().numpy()
+    for b in range(nq):
+        nt = int(ntok[b])
+        ot, osc, om, _ = O.native_prep(Q[b, :nt].numpy(), C.numpy(), 32, impute=True)
+        assert np.array_equal(topc[b, :nt], ot), f"query {b}: probed centroids differ"
+        assert np.array_equal(sc[b, :nt].view(np.uint32), osc.view(np.uint32)), f"query {b}: scores differ"
+        assert np.array_equal(m[b, :nt], om)
+    from ragrt_b200 import _lib
+    assert _lib.lib().ragrt_device_error(1) == 0
