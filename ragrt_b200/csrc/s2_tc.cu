@@ -8,19 +8,21 @@
 //            tiles of C through a ring of shared-memory stages (128-byte swizzle, K-major)
 //   warp 1 : MMA issuer -- per tile 8 x tcgen05.mma (M=128, N=128, K=16) into one of four
 //            tensor-memory accumulators (4 x 128 columns = all 512)
-//   warps 2-5 (epilogue, one per tensor-memory lane quadrant, thread = query row): drain
-//            the accumulator with tcgen05.ld, release it, then maintain the row's candidate
-//            superset.  Each fp32 accumulation brackets the exact fp16 score:
+//   warps 2-5 (epilogue, one per tensor-memory lane quadrant): drain the accumulator with
+//            tcgen05.ld and release it.  Each fp32 accumulation brackets the exact fp16 score:
 //            lo = RN16(acc - eps) <= RN16(exact) <= hi = RN16(acc + eps) (s2_common.cuh).
-//            The list is ordered by the lower-bound key (lo, centroid asc); T = its kk-th key.
-//            A value enters if its upper-bound key (hi, centroid) beats T; entries below the
-//            kk-th place survive only while their upper bound still beats T.  The exact top-kk
-//            is a subset of this superset, so no value is resolved exactly here: a 32-value
-//            chunk whose max is below the row's admission bound is skipped outright.
-// Each CTA writes its rows' supersets (KX = kk + 31 keys, bit 0 = "lo != hi") to
-// partial[query][slice][token][KX]; s2_merge_tc takes the global superset across slices,
-// resolves only its ambiguous members with an exact fp64 dot product and selects the
-// exact top-kk.  All waits are bounded; a timeout raises an error flag and every role exits.
+//            Lane l filters its row's 128 scores against the row's admission key Te (a
+//            lower bound on the row's final kk-th key); rows with survivors are then taken
+//            one at a time by the whole warp, lane = centroid, which appends superset keys
+//            (lo, centroid asc, bit 0 = "lo != hi") to the row's 64-slot list.  A full list
+//            is compacted warp-wide: bitonic sort, T = kk-th lower-bound key, keep the first
+//            kk and the entries whose upper bound still beats T (if none can be dropped,
+//            the ambiguous ones are resolved with an exact fp64 dot product first).  T is
+//            published per row with atomicMax, so the slices of a row share one admission key.
+// Each CTA writes its rows' sorted supersets to partial[query][slice][token][64];
+// s2_merge_tc takes the global superset across slices, resolves only its ambiguous
+// members with an exact fp64 dot product and selects the exact top-kk.  All waits are
+// bounded; a timeout raises an error flag and every role exits.
 #include <cuda.h>
 
 #include <algorithm>
@@ -51,7 +53,7 @@ struct S2TcParams {
     int rows_total, rows, NC, kk, tiles_total, tiles_per_slice, nslices, stages;
 };
 
-constexpr int kExtra = 31;                     // superset slots beyond kk
+constexpr int kListCap = 64;                   // per-row list slots (kk <= 63)
 
 // superset key: (ord16(lo) << 32) | ((0x7FFFFFFF - id) << 1) | ambiguous;  orders by (lo desc, id asc)
 __device__ __forceinline__ uint64_t sk_make(uint16_t lo, uint32_t id, uint32_t amb) {
@@ -70,14 +72,96 @@ __device__ __forceinline__ uint64_t sk_hi(uint64_t k) {
     return sk_make(f16_next(lo), sk_id(k), 0);
 }
 
-__device__ __forceinline__ float f16_next_mid(uint16_t h) {
-    // midpoint between fp16 h and the next larger fp16 value (h finite)
-    uint16_t n;
-    if (h == 0x8000u || h == 0) n = 1;
-    else if (h & 0x8000u) n = (uint16_t)(h - 1);
-    else n = (uint16_t)(h + 1);
-    const float a = __half2float(__ushort_as_half(h)), b = __half2float(__ushort_as_half(n));
-    return 0.5f * (a + b);
+// Score filter for admission key `te` (a lower-bound key, flag clear): a score whose fp32
+// accumulation is below the returned value rounds (with its error bound eps <= eps_max added)
+// to an fp16 value strictly below te's value, so its upper-bound key is below te whatever its
+// id.  The bound is the midpoint between te's value and the next SMALLER fp16 value.
+__device__ __forceinline__ float s2_filter_threshold(uint64_t te, float eps_max) {
+    const uint16_t h = unord16((uint32_t)(te >> 32));
+    uint16_t pv;
+    if (h == 0x8000u || h == 0) pv = 0x8001u;
+    else if (h & 0x8000u) pv = (uint16_t)(h + 1);
+    else pv = (uint16_t)(h - 1);
+    const float a = __half2float(__ushort_as_half(h)), b = __half2float(__ushort_as_half(pv));
+    const float mid = 0.5f * (a + b);
+    return mid - (eps_max + fabsf(mid) * 2.4e-7f + 1e-30f);
+}
+
+// fp16 value of the exact dot product of q and c, warp-wide (4 dims per lane; the fp64
+// partial sums of fp16 products are exact while |q||c| < 32), on every lane.
+__device__ __forceinline__ uint16_t s2_warp_exact(const __half* q, const __half* c, int lane) {
+    const uint2 qv = *reinterpret_cast<const uint2*>(q + 4 * lane);
+    const uint2 cv = __ldg(reinterpret_cast<const uint2*>(c + 4 * lane));
+    const __half* qh = reinterpret_cast<const __half*>(&qv);
+    const __half* ch = reinterpret_cast<const __half*>(&cv);
+    double d = 0.0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) d = fma((double)__half2float(qh[u]), (double)__half2float(ch[u]), d);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
+    const uint16_t h = d2h_rn(d);
+    return h == 0x8000u ? 0 : h;
+}
+
+// Bitonic sort of 64 keys held two per lane (element i = lane + 32 h), descending.
+__device__ __forceinline__ void s2_sort64_desc(uint64_t& a0, uint64_t& a1, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j == 32) {               // partner is the lane's other element (k == 64: descending)
+                const uint64_t mx = a0 > a1 ? a0 : a1, mn = a0 > a1 ? a1 : a0;
+                a0 = mx;
+                a1 = mn;
+                continue;
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint64_t& a = h ? a1 : a0;
+                const int i = lane + 32 * h;
+                const uint64_t o = __shfl_xor_sync(0xFFFFFFFFu, a, j);
+                const bool lower = (i & j) == 0, desc = (i & k) == 0;
+                const uint64_t mx = a > o ? a : o, mn = a > o ? o : a;
+                a = (lower == desc) ? mx : mn;
+            }
+        }
+    }
+}
+
+// Compact one row's list (warp-wide): optionally resolve every ambiguous entry exactly, sort
+// by key, take T = the kk-th lower-bound key (0 while fewer than kk entries), and keep the
+// first kk entries plus those whose upper bound beats T.  Returns T; updates n.
+__device__ __noinline__ uint64_t s2_compact(uint64_t* lst, int& n, int kk, bool resolve, const __half* qrow,
+                                            const __half* C, int lane) {
+    uint64_t a0 = lane < n ? lst[lane] : 0ull;
+    uint64_t a1 = lane + 32 < n ? lst[lane + 32] : 0ull;
+    if (resolve) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint64_t& a = h ? a1 : a0;
+            unsigned need = __ballot_sync(0xFFFFFFFFu, (a & 1ull) != 0);
+            while (need) {
+                const int s = __ffs(need) - 1;
+                need &= need - 1;
+                const uint32_t id = sk_id(__shfl_sync(0xFFFFFFFFu, a, s));
+                const uint16_t hx = s2_warp_exact(qrow, C + (int64_t)id * kDim, lane);
+                if (lane == s) a = sk_make(hx, id, 0);
+            }
+        }
+    }
+    s2_sort64_desc(a0, a1, lane);
+    uint64_t T = 0;
+    if (n >= kk) T = __shfl_sync(0xFFFFFFFFu, ((kk - 1) >> 5) ? a1 : a0, (kk - 1) & 31) & ~1ull;
+    const bool k0 = a0 != 0 && (lane < kk || sk_hi(a0) > T);
+    const bool k1 = a1 != 0 && (lane + 32 < kk || sk_hi(a1) > T);
+    const unsigned b0 = __ballot_sync(0xFFFFFFFFu, k0), b1 = __ballot_sync(0xFFFFFFFFu, k1);
+    const unsigned lt = (1u << lane) - 1u;
+    __syncwarp();
+    if (k0) lst[__popc(b0 & lt)] = a0;
+    if (k1) lst[__popc(b0) + __popc(b1 & lt)] = a1;
+    __syncwarp();
+    n = __popc(b0) + __popc(b1);
+    return T;
 }
 
 __global__ void __launch_bounds__(kS2TcThreads, 1)
@@ -87,9 +171,9 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     const int S = p.stages, kk = p.kk;
     uint8_t* sA = sm;
     uint8_t* sB = sm + kQTileBytes;
-    uint64_t* lists = reinterpret_cast<uint64_t*>(sB + (size_t)S * kTileBytes);    // [kk + kExtra][128]
-    float* scratch = reinterpret_cast<float*>(lists + (size_t)(kk + kExtra) * kQM); // [32][128]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + 32 * kQM);
+    uint64_t* lists = reinterpret_cast<uint64_t*>(sB + (size_t)S * kTileBytes);    // [128 rows][kListCap]
+    float* scratch = reinterpret_cast<float*>(lists + (size_t)kListCap * kQM);     // [4 warps][32][33]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + 4 * 32 * 33);
     uint64_t* fullA = bars;
     uint64_t* full = bars + 1;
     uint64_t* empty = full + S;
@@ -103,7 +187,7 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     const int t0 = slice * p.tiles_per_slice;
     const int ntiles = min(p.tiles_total, t0 + p.tiles_per_slice) - t0;
 
-    for (int i = threadIdx.x; i < (kk + kExtra) * kQM; i += blockDim.x) lists[i] = 0ull;
+    for (int i = threadIdx.x; i < kListCap * kQM; i += blockDim.x) lists[i] = 0ull;
     if (threadIdx.x == 0) {
         tc::mbar_init(fullA, 1);
         for (int s = 0; s < S; ++s) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
@@ -160,7 +244,11 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             }
         }
     } else {
-        // ------------------------------------------------------------ epilogue (thread = row)
+        // ------------------------------------------------------------ epilogue (warp-cooperative)
+        // Lane l of warp (quad) owns TMEM lane 32*quad + l = one query row: it filters that
+        // row's scores with a per-row threshold.  Rows with survivors are then handled one at a
+        // time by the whole warp (lane = centroid column), appending keys to the row's list
+        // and compacting the list (bitonic sort + trim) when it is full.
         const int quad = warp & 3;
         const int r = quad * 32 + lane;
         const int grow = rb * kQM + r;
@@ -181,20 +269,17 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             qn = __fsqrt_ru(qn) * (1.0f + 1e-6f);
         }
         const float eps_max = qn * (*p.cnmax) * kEpsTc;
-        const int KX = kk + kExtra;
-        int cnt = 0;
-        uint64_t T = 0;                       // kk-th lower-bound key (flag cleared) once cnt >= kk
-        uint64_t Te = 0;                      // admission key: max(T, best T of this row's other slices)
-        float thr_lo = -INFINITY;             // acc below this cannot produce an upper bound > Te
+        // this lane's row: list length, admission key, and the score filter derived from it
+        int n = 0;
+        uint64_t Te = 0;
+        float thr = -INFINITY;
         unsigned long long* gT = p.gthr + (valid ? grow : 0);
-        auto raise = [&](uint64_t k) {        // Te only grows; publish it and move the chunk filter
-            if (k <= Te) return;
-            Te = k;
-            const float mid = f16_next_mid(unord16((uint32_t)(Te >> 32)));
-            thr_lo = mid - (eps_max + fabsf(mid) * 2.4e-7f + 1e-30f);
-        };
+        float* sc = scratch + quad * (32 * 33);                      // [32 rows][33] of this warp
+        uint64_t* wl = lists + (size_t)quad * 32 * kListCap;        // the warp's 32 row lists
         for (int i = 0; i < ntiles; ++i) {
             const int b = i % kAccBufs;
+            // other slices' progress on this row (issued before the wait to hide its latency)
+            const unsigned long long g = valid ? *reinterpret_cast<volatile unsigned long long*>(gT) : 0ull;
             const bool ok = tc::mbar_wait_or_abort(accf + b, (i / kAccBufs) & 1, abort, kS2WaitLimit);
             if (!__all_sync(0xFFFFFFFFu, ok)) break;          // warp-uniform: tcgen05.ld is warp-collective
             tc::fence_after();
@@ -208,99 +293,111 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             tc::fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(acce + b);
-            if (!valid) continue;
-            raise(*reinterpret_cast<volatile unsigned long long*>(gT));   // other slices' progress
+            if (g > Te) {
+                Te = g;
+                thr = s2_filter_threshold(Te, eps_max);
+            }
             const int c0 = (t0 + i) * kCN;
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
-                float m16[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) m16[j] = fmaxf(__uint_as_float(v[ch][j]), __uint_as_float(v[ch][j + 16]));
-#pragma unroll
-                for (int w2 = 8; w2 >= 1; w2 >>= 1)
-#pragma unroll
-                    for (int j = 0; j < w2; ++j) m16[j] = fmaxf(m16[j], m16[j + w2]);
-                const float mx = m16[0];
-                if (!(mx >= thr_lo)) continue;
                 uint32_t cand = 0;
+                if (valid) {
+                    float m16[16];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    scratch[j * kQM + r] = __uint_as_float(v[ch][j]);
-                    cand |= (__uint_as_float(v[ch][j]) >= thr_lo) ? (1u << j) : 0u;
-                }
-                while (cand) {
-                    const int j = __ffs(cand) - 1;
-                    cand &= cand - 1;
-                    const int c = c0 + ch * 32 + j;
-                    const float acc = scratch[j * kQM + r];
-                    if (c >= p.NC || !(acc >= thr_lo)) continue;
-                    const float eps = fmaf(fabsf(acc), 1.2e-7f, qn * p.cnorm[c] * kEpsTc);
-                    const uint16_t hi = __half_as_ushort(__float2half_rn(acc + eps));
-                    if (sk_make(hi, (uint32_t)c, 0) <= Te) continue;
-                    uint16_t lo = __half_as_ushort(__float2half_rn(acc - eps));
-                    uint32_t amb = lo != hi;
-                    if (amb && f16_next(lo == 0x8000u ? 0 : lo) != (hi == 0x8000u ? 0 : hi)) {
-                        // the bracket spans more than one fp16 step (tiny scores): resolve now
-                        lo = s2_exact(qrow, p.C + (int64_t)c * kDim);
-                        amb = 0;
-                        if (sk_make(lo, (uint32_t)c, 0) <= Te) continue;
-                    }
-                    while (cnt == KX) {
-                        // full (rare): resolve the ambiguous tail entries exactly and re-rank.  Each
-                        // pass resolves at least one entry; once the tail holds only exact keys they
-                        // all rank below the kk-th entry, fall under T and are trimmed.
-                        for (int e = kk; e < cnt; ++e) {
-                            const uint64_t k = lists[e * kQM + r];
-                            if (k & 1) {
-                                const uint32_t id = sk_id(k);
-                                lists[e * kQM + r] = sk_make(s2_exact(qrow, p.C + (int64_t)id * kDim), id, 0);
-                            }
-                        }
-                        for (int e = 1; e < cnt; ++e) {
-                            const uint64_t k = lists[e * kQM + r];
-                            int q = e;
-                            while (q > 0 && lists[(q - 1) * kQM + r] < k) {
-                                lists[q * kQM + r] = lists[(q - 1) * kQM + r];
-                                --q;
-                            }
-                            lists[q * kQM + r] = k;
-                        }
-                        T = lists[(kk - 1) * kQM + r] & ~1ull;
-                        int w = kk;
-                        for (int e = kk; e < cnt; ++e) {
-                            const uint64_t k = lists[e * kQM + r];
-                            if (sk_hi(k) > T) lists[w++ * kQM + r] = k;
-                        }
-                        cnt = w;
-                    }
-                    if (sk_make(hi, (uint32_t)c, 0) <= Te || (cnt >= kk && sk_make(hi, (uint32_t)c, 0) <= T)) continue;
-                    const uint64_t key = sk_make(lo, (uint32_t)c, amb);
-                    int pos = cnt;
-                    while (pos > 0 && lists[(pos - 1) * kQM + r] < key) {
-                        lists[pos * kQM + r] = lists[(pos - 1) * kQM + r];
-                        --pos;
-                    }
-                    lists[pos * kQM + r] = key;
-                    ++cnt;
-                    if (cnt >= kk) {
-                        T = lists[(kk - 1) * kQM + r] & ~1ull;
-                        int w = kk;                   // keep tail entries whose upper bound beats T
-                        for (int e = kk; e < cnt; ++e) {
-                            const uint64_t k = lists[e * kQM + r];
-                            if (sk_hi(k) > T) lists[w++ * kQM + r] = k;
-                        }
-                        cnt = w;
-                        if (T > Te) {
-                            atomicMax(gT, (unsigned long long)T);
-                            raise(T);
-                        }
+                    for (int j = 0; j < 16; ++j)
+                        m16[j] = fmaxf(__uint_as_float(v[ch][j]), __uint_as_float(v[ch][j + 16]));
+#pragma unroll
+                    for (int w2 = 8; w2 >= 1; w2 >>= 1)
+#pragma unroll
+                        for (int j = 0; j < w2; ++j) m16[j] = fmaxf(m16[j], m16[j + w2]);
+                    if (m16[0] >= thr) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) cand |= (__uint_as_float(v[ch][j]) >= thr) ? (1u << j) : 0u;
                     }
                 }
+                unsigned act = __ballot_sync(0xFFFFFFFFu, cand != 0);
+                if (!act) continue;
+                if (cand) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sc[lane * 33 + j] = __uint_as_float(v[ch][j]);
+                }
+                __syncwarp();
+                while (act) {
+                    const int src = __ffs(act) - 1;
+                    act &= act - 1;
+                    // ---- row `src`, lane = centroid column c0 + 32 ch + lane
+                    const uint32_t cm = __shfl_sync(0xFFFFFFFFu, cand, src);
+                    int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
+                    uint64_t Te_s = __shfl_sync(0xFFFFFFFFu, Te, src);
+                    const float qn_s = __shfl_sync(0xFFFFFFFFu, qn, src);
+                    const __half* qrow_s = p.Q + (int64_t)(rb * kQM + quad * 32 + src) * kDim;
+                    uint64_t* lst = wl + src * kListCap;
+                    const int c = c0 + ch * 32 + lane;
+                    bool adm = ((cm >> lane) & 1u) && c < p.NC;
+                    uint64_t key = 0;
+                    if (adm) {
+                        const float acc = sc[src * 33 + lane];
+                        const float eps = fmaf(fabsf(acc), 1.2e-7f, qn_s * __ldg(p.cnorm + c) * kEpsTc);
+                        uint16_t hi = __half_as_ushort(__float2half_rn(acc + eps));
+                        if (hi == 0x8000u) hi = 0;
+                        if (sk_make(hi, (uint32_t)c, 0) <= Te_s) {
+                            adm = false;
+                        } else {
+                            uint16_t lo = __half_as_ushort(__float2half_rn(acc - eps));
+                            if (lo == 0x8000u) lo = 0;
+                            uint32_t amb = lo != hi;
+                            if (amb && f16_next(lo) != hi) {
+                                // the bracket spans more than one fp16 step (tiny scores): resolve now
+                                lo = s2_exact(qrow_s, p.C + (int64_t)c * kDim);
+                                amb = 0;
+                                if (sk_make(lo, (uint32_t)c, 0) <= Te_s) adm = false;
+                            }
+                            key = sk_make(lo, (uint32_t)c, amb);
+                        }
+                    }
+                    bool raised = false;
+                    unsigned am = __ballot_sync(0xFFFFFFFFu, adm);
+                    while (am) {
+                        const int room = kListCap - n_s;
+                        if (room == 0) {
+                            uint64_t T = s2_compact(lst, n_s, kk, false, qrow_s, p.C, lane);
+                            if (n_s == kListCap) T = s2_compact(lst, n_s, kk, true, qrow_s, p.C, lane);
+                            if (T > Te_s) { Te_s = T; raised = true; }
+                            if (adm && sk_hi(key) <= Te_s) adm = false;
+                            am = __ballot_sync(0xFFFFFFFFu, adm);
+                            continue;
+                        }
+                        const int rank = __popc(am & ((1u << lane) - 1u));
+                        const bool take = adm && rank < room;
+                        if (take) lst[n_s + rank] = key;
+                        n_s += min(__popc(am), room);
+                        adm = adm && !take;
+                        am = __ballot_sync(0xFFFFFFFFu, adm);
+                    }
+                    __syncwarp();
+                    if (raised && lane == 0) atomicMax(p.gthr + (rb * kQM + quad * 32 + src), (unsigned long long)Te_s);
+                    if (lane == src) {
+                        n = n_s;
+                        if (Te_s > Te) {
+                            Te = Te_s;
+                            thr = s2_filter_threshold(Te, eps_max);
+                        }
+                    }
+                }
+                __syncwarp();
             }
         }
-        if (valid) {
-            uint64_t* out = p.partial + (((int64_t)qb * p.nslices + slice) * p.rows + tok) * (kk + kExtra);
-            for (int j = 0; j < kk + kExtra; ++j) out[j] = j < cnt ? lists[j * kQM + r] : 0ull;
+        // ---- every valid row: final compaction (sorted, trimmed) and write-out
+        for (int src = 0; src < 32; ++src) {
+            if (!__shfl_sync(0xFFFFFFFFu, valid, src)) continue;
+            int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
+            const int grow_s = rb * kQM + quad * 32 + src;
+            uint64_t* lst = wl + src * kListCap;
+            s2_compact(lst, n_s, kk, false, p.Q + (int64_t)grow_s * kDim, p.C, lane);
+            const int qb_s = grow_s / p.rows, tok_s = grow_s % p.rows;
+            uint64_t* out = p.partial + (((int64_t)qb_s * p.nslices + slice) * p.rows + tok_s) * kListCap;
+            out[lane] = lane < n_s ? lst[lane] : 0ull;
+            out[lane + 32] = lane + 32 < n_s ? lst[lane + 32] : 0ull;
         }
     }
     __syncthreads();
@@ -473,12 +570,12 @@ static int make_map(CUtensorMap* m, const void* base, int64_t rows) {
 }
 
 static size_t s2_tc_smem(int kk, int stages) {
-    return 1024 + kQTileBytes + (size_t)stages * kTileBytes + (size_t)(kk + kExtra) * kQM * 8 + 32 * kQM * 4 +
+    return 1024 + kQTileBytes + (size_t)stages * kTileBytes + (size_t)kListCap * kQM * 8 + 4 * 32 * 33 * 4 +
            8 * (1 + 2 * stages + 2 * kAccBufs) + 16;
 }
 
 bool s2_tc_supported(int kk, int64_t rows_total) {
-    return rows_total >= kQM && kk <= 64 && s2_tc_smem(kk, 2) <= 227 * 1024;
+    return rows_total >= kQM && kk < kListCap && s2_tc_smem(kk, 2) <= 227 * 1024;
 }
 
 void s2_tc_plan(int B, int rows, int NC, int& nslices, int& tiles_per_slice) {
@@ -494,7 +591,7 @@ void s2_tc_plan(int B, int rows, int NC, int& nslices, int& tiles_per_slice) {
 size_t s2_tc_partial_bytes(int B, int rows, int NC, int kk) {
     int ns, tps;
     s2_tc_plan(B, rows, NC, ns, tps);
-    return sizeof(uint64_t) * (size_t)B * ns * rows * (kk + kExtra) + sizeof(uint64_t) * (size_t)B * rows + 256;
+    return sizeof(uint64_t) * (size_t)B * ns * rows * kListCap + sizeof(uint64_t) * (size_t)B * rows + 256;
 }
 
 int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __half* C, int NC, const float* cnorm,
@@ -511,7 +608,7 @@ int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __hal
     while (stages > 2 && s2_tc_smem(kk, stages) > 227 * 1024) --stages;
     const size_t smem = s2_tc_smem(kk, stages);
     unsigned long long* gthr = reinterpret_cast<unsigned long long*>(
-        partial + (size_t)B * nslices * rows * (kk + kExtra));
+        partial + (size_t)B * nslices * rows * kListCap);
     RAGRT_CUDA_TRY(cudaMemsetAsync(gthr, 0, sizeof(uint64_t) * (size_t)B * rows, stream));
     S2TcParams p{Q, C, cnorm, cnmax, ntok, partial, gthr, err, B * rows, rows, NC, kk, (int)ceil_div(NC, kCN), tps,
                  nslices, stages};
@@ -519,7 +616,7 @@ int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __hal
     dim3 grid(nslices, (unsigned)ceil_div((int64_t)B * rows, kQM));
     s2_tc<<<grid, kS2TcThreads, smem, stream>>>(tmQ, tmC, p);
     RAGRT_LAUNCH_CHECK();
-    const int KX = kk + kExtra;
+    const int KX = kListCap;
     const int warps = 4;
     const size_t msmem = sizeof(uint64_t) * warps * ((size_t)nslices * KX + kk);
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_merge_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
