@@ -94,6 +94,24 @@ int ragrt_centroid_topk(const void* d_Q, const int32_t* d_ntok, int32_t B, int32
                         int32_t* d_topc, float* d_scores, float* d_m, void* d_full16, void* stream);
 
 /*
+ * Stage 2 without any memory allocation.  No counterpart in the reference: it exists for
+ * callers that must not allocate device memory per call.  Same arguments and bit-identical
+ * outputs as ragrt_centroid_topk with d_full16 = NULL, but the scratch lives in one static
+ * 32 MiB device array per device instead of cudaMallocAsync/cudaFreeAsync.
+ *   - The first call on a device (with it current) looks up the array's address
+ *     (cudaGetSymbolAddress; may load the module): make it before any stream capture.
+ *   - A call that needs more than 32 MiB of scratch (about B x rows x 520 bytes on the
+ *     tensor-core path at nc = 32, plus 4 bytes per centroid) returns RAGRT_ERR_ARG.
+ *   - All calls on a device share the array: calls that overlap on the GPU race.
+ * ragrt_centroid_topk_noalloc_error reads (and with reset != 0 clears) the error word that
+ * the tensor-core kernel sets when one of its bounded waits gives up (synchronous).
+ */
+int ragrt_centroid_topk_noalloc(const void* d_Q, const int32_t* d_ntok, int32_t B, int32_t rows,
+                                const void* d_C, int32_t NC, int32_t nc, int32_t impute,
+                                int32_t* d_topc, float* d_scores, float* d_m, void* stream);
+int ragrt_centroid_topk_noalloc_error(int32_t reset);
+
+/*
  * Stages 1-3 in `weft` mode for B queries: every chunk (eid < n_eids) of every probed
  * centroid whose base score is > 0, per (passage, token) the max fp16 base score, per
  * passage the sum over tokens, then candidate selection.  Replaces the all-codewords

@@ -38,6 +38,8 @@ _SIGS = {
     "ragrt_index_create": (I32, [C.POINTER(IndexDesc), C.POINTER(P), P]),
     "ragrt_index_destroy": (I32, [P]),
     "ragrt_centroid_topk": (I32, [P, P, I32, I32, P, I32, I32, I32, P, P, P, P, P]),
+    "ragrt_centroid_topk_noalloc": (I32, [P, P, I32, I32, P, I32, I32, I32, P, P, P, P]),
+    "ragrt_centroid_topk_noalloc_error": (I32, [I32]),
     "ragrt_weft_candidates": (I32, [P, P, P, I32, P, I32, I32, I32, I32, P, I32, P, P, P, P]),
     "ragrt_tile_maxsim": (I32, [P, P, I32, I32, P, P, I32, P, P, P, P, P, P, P, I32, P]),
     "ragrt_final_topk": (I32, [P, P, I32, I32, P, I32, P, I32, P, P, P]),
