@@ -61,6 +61,15 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+def load_traffic():
+    """Per-unit DRAM traffic of the dominant kernels from the committed ncu summaries."""
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
 def load_peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -164,18 +173,10 @@ def build_workload(cfg, rank, world, seed=0):
     corp = synth.make_corpus(cfg["num_docs"], centres, cents, len_range=cfg["len_range"], seed=seed, device=dev)
     preds = synth.make_predicates(cfg["num_docs"], seed=1, device=dev)
     N = cfg["num_docs"]
-    lo = (N * rank) // world
-    hi = (N * (rank + 1)) // world
-    off = corp["doc_offsets"]
-    t_lo, t_hi = int(off[lo]), int(off[hi])
-    shard = {
-        "doclens": corp["doclens"][lo:hi].contiguous(),
-        "doc_offsets": (off[lo:hi + 1] - t_lo).contiguous(),
-        "codes": corp["codes"][t_lo:t_hi].contiguous(),
-        "residuals": corp["residuals"][t_lo:t_hi].contiguous(),
-        "preds": preds[lo:hi].contiguous(),
-        "pid_base": lo,
-    }
+    from ragrt_b200.shard import shard_range, slice_docs
+    lo, hi = shard_range(N, rank, world)
+    shard = slice_docs(corp["doc_offsets"], corp["doclens"], corp["codes"], corp["residuals"], preds, lo, hi)
+    t_lo, t_hi = int(corp["doc_offsets"][lo]), int(corp["doc_offsets"][hi])
     del corp["codes"], corp["residuals"]
     torch.cuda.empty_cache()
     ix = index_build.plain_ivf_index(shard["codes"], shard["doclens"], cents.shape[0])
@@ -266,18 +267,8 @@ def make_masks(cfg, B):
 # ----------------------------------------------------------------------------- ours
 def merge_shards(ids, sc, world, k_top, pid_base):
     """All-gather per-shard top-k (score, global pid) and merge (score desc, pid asc)."""
-    import torch.distributed as dist
-    gpid = torch.where(ids >= 0, ids + pid_base, ids)
-    pack = torch.stack([sc, gpid.to(torch.float32)], 0)              # pids < 2^24: exact in fp32
-    out = torch.empty(world, *pack.shape, dtype=pack.dtype, device=pack.device)
-    dist.all_gather_into_tensor(out, pack)
-    scores = out[:, 0].permute(1, 0, 2).reshape(ids.shape[0], -1)
-    pids = out[:, 1].permute(1, 0, 2).reshape(ids.shape[0], -1).to(torch.int64)
-    key = torch.where(pids >= 0, pids, torch.full_like(pids, 1 << 40))
-    order = torch.argsort(key, dim=1, stable=True)                    # pid asc ...
-    scores, pids = torch.gather(scores, 1, order), torch.gather(pids, 1, order)
-    order = torch.argsort(scores, dim=1, descending=True, stable=True)  # ... then score desc
-    return torch.gather(pids, 1, order)[:, :k_top], torch.gather(scores, 1, order)[:, :k_top]
+    from ragrt_b200.shard import merge_topk
+    return merge_topk(ids, sc, world, k_top, pid_base)
 
 
 def run_ours(args, cfg, rank, world, local):
@@ -293,8 +284,11 @@ def run_ours(args, cfg, rank, world, local):
     sc = torch.empty(nb, B, k_top, dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()
 
+    # events at the stage boundaries of every timed step, on the launching stream
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(nb)]
+
     def step(i):
-        wix.search(Q[i], nc=nc, K=K, k_top=k_top, masks=masks, out=(ids[i], sc[i]))
+        wix.search_profiled(Q[i], ev[i], nc=nc, K=K, k_top=k_top, masks=masks, out=(ids[i], sc[i]))
         if world > 1:
             merge_shards(ids[i], sc[i], world, k_top, shard["pid_base"])
 
@@ -342,23 +336,21 @@ def run_ours(args, cfg, rank, world, local):
     ms_e2e = max_over_ranks(e2.elapsed_time(e3), world)
     e2e = B * args.steps / (ms_e2e / 1000.0)
 
-    # ---- stage breakdown: events at the stage boundaries on the launching stream
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
-    cand_tokens = 0
-    wix.stats(reset=True)
-    torch.cuda.synchronize()
-    for j, i in enumerate(range(args.warmup, nb)):
-        wix.search_profiled(Q[i], ev[j], nc=nc, K=K, k_top=k_top, masks=masks, out=(ids[i], sc[i]))
-    torch.cuda.synchronize()
-    st2 = wix.stats()
-    stage_ms = np.array([[ev[j][s].elapsed_time(ev[j][s + 1]) for s in range(4)] for j in range(args.steps)])
+    # ---- stage breakdown of the timed steps (events recorded inside the timed region)
+    st2 = stats
+    stage_ms = np.array([[ev[i][s].elapsed_time(ev[i][s + 1]) for s in range(4)] for i in range(args.warmup, nb)])
     stage_ms = stage_ms.mean(0)
-    # Stage-4 algorithmic work: candidates and their tokens (one query batch, same K)
-    topc, s2sc, _, _ = wix.centroid_topk(Q[args.warmup], nc)
-    cp, _, _ = wix.candidates(topc, s2sc, K, masks=masks)
-    valid = cp >= 0
-    cand_tokens = int(wix.doc_lens[cp[valid].long()].sum())
-    n_cand = int(valid.sum())
+    # Stage-4 algorithmic work per launch: candidates and their doc tokens, averaged over the
+    # timed batches (recomputed after the timed region)
+    cand_tokens = n_cand = 0
+    for i in range(args.warmup, nb):
+        topc, s2sc, _, _ = wix.centroid_topk(Q[i], nc)
+        cp, _, _ = wix.candidates(topc, s2sc, K, masks=masks)
+        valid = cp >= 0
+        cand_tokens += int(wix.doc_lens[cp[valid].long()].sum())
+        n_cand += int(valid.sum())
+    cand_tokens //= args.steps
+    n_cand //= args.steps
     peaks, peak_kind = load_peaks()
     s2_flops = 2.0 * B * 32 * wix.NC * 128
     s3_bytes = (3.0 * st2["distinct_postings"] + 8.0 * st2["touched"]) / args.steps
@@ -369,11 +361,12 @@ def run_ours(args, cfg, rank, world, local):
                              "work": f"{s2_flops / 1e9:.1f} GFLOP/step"},
         "s3_aggregate": {"ms": stage_ms[1], "achieved": s3_bytes / (stage_ms[1] / 1e3) / 1e9, "unit": "GB/s",
                          "peak": peaks["hbm_gbs"], "bound": "hbm",
-                         "work": f"{s3_bytes / 1e6:.1f} MB/step (3 B x distinct postings + 8 B x touched)"},
+                         "work": f"{s3_bytes / 1e6:.1f} MB/step (3 B x distinct postings + 8 B x touched)",
+                         "algorithmic": s3_bytes / 1e9},
         "s4_maxsim": {"ms": stage_ms[2], "achieved": s4_bytes / (stage_ms[2] / 1e3) / 1e9, "unit": "GB/s",
                       "peak": peaks["hbm_gbs"], "bound": "hbm",
                       "work": f"{s4_bytes / 1e6:.1f} MB/step (36 B x {cand_tokens:,} doc tokens + 16 B x cand)",
-                      "doc_tokens_per_s": cand_tokens / (stage_ms[2] / 1e3)},
+                      "doc_tokens_per_s": cand_tokens / (stage_ms[2] / 1e3), "algorithmic": s4_bytes / 1e9},
         "final_topk": {"ms": stage_ms[3]},
     }
     for s in stages.values():
@@ -381,8 +374,14 @@ def run_ours(args, cfg, rank, world, local):
             s["frac"] = s["achieved"] / s["peak"]
     dom = max(("s2_centroid_topk", "s3_aggregate", "s4_maxsim"), key=lambda k: stages[k]["ms"])
     d = stages[dom]
+    traffic = None
+    tr = load_traffic().get(dom)
+    if tr and "dram_bytes_per_doc_token" in tr:
+        traffic = tr["dram_bytes_per_doc_token"] * cand_tokens / 1e9       # GB per launch, scaled
     roofline = {"bound": d["bound"], "achieved": d["achieved"], "peak": d["peak"], "unit": d["unit"],
-                "frac": d["frac"], "traffic": None, "kernel": dom, "peak_source": peak_kind}
+                "frac": d["frac"], "traffic": traffic, "traffic_unit": "GB per launch" if traffic else None,
+                "algorithmic": d.get("algorithmic"), "kernel": dom, "peak_source": peak_kind,
+                "timing": "CUDA events at stage boundaries inside the timed region, mean over steps"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

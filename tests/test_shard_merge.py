@@ -1,0 +1,110 @@
+"""Doc-range sharding on CPU with world_size-2 `gloo` ranks: every rank slices its shard of a
+small corpus, runs the CPU restatement of the whole path (oracle) on it, and merges the
+per-shard top-k with ragrt_b200.shard.merge_topk (the same function bench.py runs over NCCL).
+The merged list must equal the single-process merge of both shards' results by (score desc,
+global pid asc), on every rank."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from ragrt_b200 import index_build, shard
+from tests.helpers import small_corpus, oracle_index
+
+WORLD = 2
+K_TOP = 10
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _shard_search(rank, world):
+    d, Q, E, _ = small_corpus()
+    N = d["doc_lens"].shape[0]
+    lo, hi = shard.shard_range(N, rank, world)
+    sh = shard.slice_docs(d["doc_offsets"], d["doc_lens"], d["codes"], d["residuals"], d["doc_predicates"], lo, hi)
+    ix = index_build.plain_ivf_index(sh["codes"], sh["doclens"], d["centroids"].shape[0])
+    ds = dict(d)
+    ds.update({"csr_row_ptrs": ix["csr_row_ptrs"], "csr_col_eids": ix["csr_col_eids"],
+               "csr_block_sums": ix["csr_block_sums"], "csr_lengths": ix["csr_lengths"],
+               "csr_packed_24": ix["csr_packed_24"], "doc_offsets": sh["doc_offsets"], "doc_lens": sh["doclens"],
+               "codes": sh["codes"], "residuals": sh["residuals"], "doc_predicates": sh["preds"]})
+    from oracle import oracle as O
+    B = Q.shape[0]
+    ntok = np.full(B, 32, np.int32)
+    ids, sc, _ = O.weft_search(oracle_index(ds), Q.reshape(B, 32, 128).numpy(), ntok, 8, ix["E"], None,
+                               200, K_TOP, nthreads=1)
+    return ids, sc, lo
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ids, sc, lo = _shard_search(rank, world)
+        g_ids, g_sc = shard.merge_topk(torch.from_numpy(ids), torch.from_numpy(sc), world, K_TOP, lo)
+        q.put((rank, g_ids.numpy(), g_sc.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _expected(world):
+    per = [_shard_search(r, world) for r in range(world)]
+    B = per[0][0].shape[0]
+    out_ids = np.full((B, K_TOP), -1, np.int64)
+    out_sc = np.full((B, K_TOP), -np.inf, np.float32)
+    for b in range(B):
+        items = []
+        for ids, sc, lo in per:
+            for j in range(ids.shape[1]):
+                pid = int(ids[b, j])
+                items.append((float(sc[b, j]), pid + lo if pid >= 0 else -1))
+        items.sort(key=lambda t: (-t[0], t[1] if t[1] >= 0 else 1 << 40))
+        for j, (s, p) in enumerate(items[:K_TOP]):
+            out_sc[b, j], out_ids[b, j] = s, p
+    return out_ids, out_sc
+
+
+def test_slice_docs_covers_corpus():
+    d, _, _, _ = small_corpus()
+    N = d["doc_lens"].shape[0]
+    toks = 0
+    for r in range(3):
+        lo, hi = shard.shard_range(N, r, 3)
+        sh = shard.slice_docs(d["doc_offsets"], d["doc_lens"], d["codes"], d["residuals"], d["doc_predicates"], lo, hi)
+        assert int(sh["doc_offsets"][0]) == 0 and int(sh["doc_offsets"][-1]) == sh["codes"].shape[0]
+        assert torch.equal(sh["codes"], d["codes"][int(d["doc_offsets"][lo]):int(d["doc_offsets"][hi])])
+        toks += sh["codes"].shape[0]
+    assert toks == d["codes"].shape[0]
+
+
+def test_two_rank_gloo_merge_matches_single_process():
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(WORLD):
+        r, ids, sc = q.get(timeout=180)
+        got[r] = (ids, sc)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    exp_ids, exp_sc = _expected(WORLD)
+    for r in range(WORLD):
+        np.testing.assert_array_equal(got[r][0], exp_ids)
+        np.testing.assert_array_equal(got[r][1], exp_sc)
+    # the merge really mixes both shards
+    assert (exp_ids >= shard.shard_range(small_corpus()[0]["doc_lens"].shape[0], 1, WORLD)[0]).any()
