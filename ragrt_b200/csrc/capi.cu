@@ -99,7 +99,8 @@ static int weft_search_impl(ragrt_index* ix, const void* d_Q, const int32_t* d_n
                 nullptr, s3ws, s3b, stream);
     if (rc || (rc = mark(2))) return rc;
     S4Docs D{ix->d.doc_offsets, ix->d.doc_lens, ix->d.codes, ix->d.residuals, (const __half*)ix->d.centroids,
-             (const __half*)ix->d.bucket_weights, ix->d.reversed_bit_map, ix->d.decomp_table, ix->d.num_passages};
+             (const __half*)ix->d.bucket_weights, ix->d.reversed_bit_map, ix->d.decomp_table, ix->d.num_passages,
+             ix->d.num_centroids};
     rc = rerank_mode == 1 ? s4_tc_launch((const __half*)d_Q, cand, B, K, D, fsc, stream)
                           : s4_simt_launch((const __half*)d_Q, cand, B, K, D, fsc, stream);
     if (rc || (rc = mark(3))) return rc;

@@ -31,6 +31,7 @@ namespace ragrt {
 
 constexpr int kS3Warps = 8;
 constexpr int kS3Threads = kS3Warps * 32;
+constexpr int kS3Batch = 8;       // 32-posting chunks whose pid loads a warp keeps in flight together
 
 struct S3Params {
     // index
@@ -68,8 +69,10 @@ s3_accumulate(S3Params p) {
     unsigned long long* sums = reinterpret_cast<unsigned long long*>(s3_smem);          // [W]
     uint32_t* seen = reinterpret_cast<uint32_t*>(sums + W);                              // [warps][W/32]
     uint16_t* touched = reinterpret_cast<uint16_t*>(seen + kS3Warps * (W >> 5));         // [W]
-    int32_t* pc = reinterpret_cast<int32_t*>(touched + W);                               // [32][kc]
-    uint16_t* pv = reinterpret_cast<uint16_t*>(pc + kRows * p.kc);                       // [32][kc]
+    int64_t* pcs = reinterpret_cast<int64_t*>(touched + W);                              // [32][kc] cstart
+    int32_t* pc = reinterpret_cast<int32_t*>(pcs + kRows * p.kc);                        // [32][kc] centroid
+    int32_t* pcnt = pc + kRows * p.kc;                                                   // [32][kc] postings
+    uint16_t* pv = reinterpret_cast<uint16_t*>(pcnt + kRows * p.kc);                     // [32][kc] fp16 bits
     __shared__ int s_np[kRows];
     __shared__ unsigned s_ntouched;
     __shared__ unsigned s_unit;
@@ -114,8 +117,12 @@ s3_accumulate(S3Params p) {
                         unsigned bal = __ballot_sync(0xFFFFFFFFu, keep);
                         if (keep) {
                             int slot = n + __popc(bal & ((1u << lane) - 1));
+                            const int nl = min(p.clists[c], p.n_eids);
+                            const int64_t cs = p.cstart[c];
                             pc[t * p.kc + slot] = c;
                             pv[t * p.kc + slot] = f2h_pos15(base);
+                            pcs[t * p.kc + slot] = cs;
+                            pcnt[t * p.kc + slot] = nl > 0 ? (int32_t)(p.list_off[p.rp[c] + nl] - cs) : 0;
                         }
                         n += __popc(bal);
                     }
@@ -141,13 +148,11 @@ s3_accumulate(S3Params p) {
                 if (j < np) {
                     const int c = pc[t * p.kc + j];
                     v = pv[t * p.kc + j];
-                    const int nl = min(p.clists[c], p.n_eids);
-                    const int64_t cs = p.cstart[c];
-                    const int64_t cnt = nl > 0 ? p.list_off[p.rp[c] + nl] - cs : 0;
+                    const int64_t cnt = pcnt[t * p.kc + j];
                     const uint32_t* bo = p.boff + (int64_t)c * (p.R + 1) + r;
                     const int64_t hi = (int64_t)bo[1] < cnt ? (int64_t)bo[1] : cnt;
                     const int64_t lo = (int64_t)bo[0] < hi ? (int64_t)bo[0] : hi;
-                    start = cs + lo;
+                    start = pcs[t * p.kc + j] + lo;
                     len = (int)(hi - lo);
                 }
                 // inclusive scan of len over the group
@@ -160,36 +165,47 @@ s3_accumulate(S3Params p) {
                 const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
                 const int excl = incl - len;
                 st_post += (unsigned long long)len;
-                for (int e0 = 0; e0 < total; e0 += 32) {
-                    const int e = e0 + lane;
-                    // source probe: the last lane whose exclusive prefix is <= e
-                    int src = 0;
+                // kS3Batch chunks of 32 postings at a time: all their pid (and predicate) loads
+                // are issued before the first chunk is merged, in posting order
+                for (int e0 = 0; e0 < total; e0 += 32 * kS3Batch) {
+                    int32_t pid[kS3Batch];
+                    uint16_t vb[kS3Batch];
 #pragma unroll
-                    for (int step = 16; step; step >>= 1) {
-                        int cand = src + step;
-                        int ex = __shfl_sync(0xFFFFFFFFu, excl, cand & 31);
-                        if (cand < 32 && ex <= e) src = cand;
+                    for (int u = 0; u < kS3Batch; ++u) {
+                        const int e = e0 + 32 * u + lane;
+                        // source probe: the last lane whose exclusive prefix is <= e
+                        int src = 0;
+#pragma unroll
+                        for (int step = 16; step; step >>= 1) {
+                            int cand = src + step;
+                            int ex = __shfl_sync(0xFFFFFFFFu, excl, cand & 31);
+                            if (cand < 32 && ex <= e) src = cand;
+                        }
+                        const int ex_src = __shfl_sync(0xFFFFFFFFu, excl, src);
+                        const int64_t st_src = __shfl_sync(0xFFFFFFFFu, start, src);
+                        vb[u] = (uint16_t)__shfl_sync(0xFFFFFFFFu, (int)v, src);
+                        pid[u] = e < total ? load_pid24(p.packed, st_src + (e - ex_src)) : -1;
                     }
-                    const int ex_src = __shfl_sync(0xFFFFFFFFu, excl, src);
-                    const int64_t st_src = __shfl_sync(0xFFFFFFFFu, start, src);
-                    const uint16_t v_src = (uint16_t)__shfl_sync(0xFFFFFFFFu, (int)v, src);
-                    bool ok = e < total;
-                    int local = -1;
-                    if (ok) {
-                        const int32_t pid = load_pid24(p.packed, st_src + (e - ex_src));
-                        local = (int)(pid - range_lo);
-                        ok = pid < p.N && local >= 0 && local < W;
-                        if (ok && mask) ok = (p.preds[pid] & mask) != 0u;   // ragrt_fused_kernel.cu:387
-                    }
-                    const int key = ok ? local : (0x40000000 | lane);
-                    const unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
-                    if (ok && lane == __ffs(peers) - 1) {
-                        const uint32_t bit = 1u << (local & 31);
-                        const uint32_t old = atomicOr(&my_seen[local >> 5], bit);
-                        if (!(old & bit)) {
-                            const unsigned long long add = (h_fixed24(v_src) << 6) | 1ull;
-                            const unsigned long long prev = atomicAdd(&sums[local], add);
-                            if (prev == 0ull) touched[atomicAdd(&s_ntouched, 1u)] = (uint16_t)local;
+                    uint32_t pr[kS3Batch];
+#pragma unroll
+                    for (int u = 0; u < kS3Batch; ++u)
+                        pr[u] = (mask && pid[u] >= 0 && pid[u] < p.N) ? p.preds[pid[u]] : 0xFFFFFFFFu;
+#pragma unroll
+                    for (int u = 0; u < kS3Batch; ++u) {
+                        if (e0 + 32 * u >= total) break;                    // warp-uniform
+                        const int local = pid[u] - (int)range_lo;
+                        bool ok = pid[u] >= 0 && pid[u] < p.N && local >= 0 && local < W;
+                        if (ok && mask) ok = (pr[u] & mask) != 0u;         // ragrt_fused_kernel.cu:387
+                        const int key = ok ? local : (0x40000000 | lane);
+                        const unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
+                        if (ok && lane == __ffs(peers) - 1) {
+                            const uint32_t bit = 1u << (local & 31);
+                            const uint32_t old = atomicOr(&my_seen[local >> 5], bit);
+                            if (!(old & bit)) {
+                                const unsigned long long add = (h_fixed24(vb[u]) << 6) | 1ull;
+                                const unsigned long long prev = atomicAdd(&sums[local], add);
+                                if (prev == 0ull) touched[atomicAdd(&s_ntouched, 1u)] = (uint16_t)local;
+                            }
                         }
                     }
                 }
@@ -296,7 +312,7 @@ int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_s
     unsigned int* work = (unsigned int*)wsp;
 
     const size_t smem = sizeof(unsigned long long) * W + sizeof(uint32_t) * kS3Warps * (W >> 5) +
-                        sizeof(uint16_t) * W + (sizeof(int32_t) + sizeof(uint16_t)) * kRows * kc + 16;
+                        sizeof(uint16_t) * W + (sizeof(int64_t) + 2 * sizeof(int32_t) + sizeof(uint16_t)) * kRows * kc + 16;
     if (smem > 220 * 1024) return fail(RAGRT_ERR_CAPACITY, "stage-3 tile needs %zu bytes of shared memory", smem);
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s3_accumulate, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;

@@ -14,6 +14,7 @@ struct S4Docs {
     const uint8_t* rbm;
     const uint8_t* decomp;
     int N;
+    int NC;           // centroid rows (codes outside [0, NC) are rejected in-kernel); INT32_MAX = unchecked
 };
 
 int s4_simt_launch(const __half* Q, const int32_t* pids, int B, int n, const S4Docs& D, float* out,

@@ -171,7 +171,7 @@ extern "C" int ragrt_tile_maxsim(const void* d_Q, const int32_t* d_pids, int32_t
     RAGRT_REQUIRE(((uintptr_t)d_Q & 15) == 0 && ((uintptr_t)d_residuals & 15) == 0 &&
                   ((uintptr_t)d_centroids & 15) == 0, "Q, residuals and centroids must be 16-byte aligned");
     S4Docs D{d_doc_offsets, d_doc_lens, d_codes, d_residuals, (const __half*)d_centroids,
-             (const __half*)d_bucket_weights, d_reversed_bit_map, d_decomp_table, num_passages};
+             (const __half*)d_bucket_weights, d_reversed_bit_map, d_decomp_table, num_passages, INT32_MAX};
     if (mode == 1) return s4_tc_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
     return s4_simt_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
 }

@@ -2,53 +2,62 @@
 // 2-bit residual decompression + TileMaxSim.  Replaces the reference's wmma kernel
 // (tile_maxsim_fused_decomp.cu:125-229), same result definition:
 //   score(pid) = sum_r max_t (q_r . d_t) * rsqrt(|d_t|^2 + 1e-12)
+// with d_t = fp16(centroid[code_t] + bucket_weight[bucket of dim]) per dim.
 //
-// One MMA tile = M 128 doc tokens x N 32 query rows x K 128 dims:
-//   * A = decoded doc tokens, written from registers straight into TENSOR MEMORY
-//     (tcgen05.st): the thread that decodes a token owns its TMEM lane, so decoded tokens
-//     never touch shared memory.  Lanes 32q..32q+31 (quadrant q) hold 32 consecutive tokens
-//     of ONE candidate of the warp that owns quadrant q.
-//   * B = the query's 32 x 128 fp16 rows in shared memory (128-byte swizzle, K-major).
-//   * D = 128 x 32 fp32 in tensor memory; each warp reads back its own quadrant.
-//   * |d_t|^2 also runs on the tensor core: A2 = d*d (fp16) times a ones matrix (N = 16);
-//     column 0 of that accumulator is the squared norm of the lane's token.
-// A CTA runs two independent tile groups (4 warps each, 176 TMEM columns each) so one
-// group's decode overlaps the other's MMA and epilogue, and every warp software-pipelines
-// its gathers: the code of chunk i+2 and the centroid rows / residual bytes of chunk i+1
-// are in flight while chunk i is stored, multiplied and reduced.
-// Epilogue per warp: scale the 32 dot products of its lane's token by the inverse norm,
-// max over the chunk's 32 tokens (= lanes) with redux.sync.max.f32 per query row, a
-// running max per candidate in the lane of that row, and the sum over rows when the
-// candidate's last chunk is done.  All waits are bounded; a timeout raises the device
-// error flag and the CTA exits.
+// Warp-specialised pipeline, one CTA per SM, 256 candidates per CTA in 4 streams (stream q
+// = candidates q, q+4, ...; chunks of 32 tokens, one candidate per chunk).  Tile k of the
+// CTA holds chunk k of every stream, stream q in tensor-memory lane quadrant q:
+//   * 8 decoder warps (warp w: quadrant w % 4, tiles k = w / 4 mod 2).  For its next chunk a
+//     decoder issues coalesced 16-byte cp.async copies (a half-warp per 256-byte centroid
+//     row) into a padded shared-memory staging buffer, then decodes its current chunk with
+//     lane = token: d = hadd(centroid, LUT[residual byte]) (16-way replicated byte LUT) and
+//     d*d, written to tensor memory with tcgen05.st (A and A2 of the decoder's A slot).
+//   * 1 MMA thread: per tile, tcgen05.mma with A from tensor memory: D = A.Q^T (N = 32) and
+//     D2 = A2.1 (N = 16, column 0 = |d|^2) into one of 4 accumulator slots.
+//   * 4 epilogue warps (quadrant q): tcgen05.ld of the chunk's 32 tokens x 32 query rows and
+//     the norms, scale by rsqrt(|d|^2 + 1e-12), max over tokens per row (redux.sync.max.f32),
+//     running max per candidate, sum over rows after the candidate's last chunk.
+// mbarriers: afull[2] (decoders -> MMA), aempty[2] (MMA done reading A), dfull[4] (MMA ->
+// epilogue), dempty[4] (epilogue done reading D).  All waits are bounded; a timeout raises
+// the device error flag, every role leaves its loop, copies and MMAs in flight are awaited
+// (bounded) and tensor memory is freed.
 #include "common.cuh"
 #include "s4_common.cuh"
 #include "tc.cuh"
 
 namespace ragrt {
 
-constexpr int kGroups = 2;
-constexpr int kGroupWarps = 4;
-constexpr int kTcThreads = kGroups * kGroupWarps * 32;
-constexpr int kStreams = kGroups * kGroupWarps;     // candidate streams per CTA (one per warp)
+constexpr int kDecWarps = 8;
+constexpr int kMmaWarp = kDecWarps;                   // warp 8
+constexpr int kTcThreads = (kDecWarps + 1 + 4) * 32;  // 416
 constexpr int kTcCandPerCta = 256;
-constexpr uint32_t kColA = 0;      // 64 columns: 128 fp16 dims per token lane
-constexpr uint32_t kColA2 = 64;    // 64 columns: squared dims
-constexpr uint32_t kColD = 128;    // 32 columns: dot products with the 32 query rows
-constexpr uint32_t kColD2 = 160;   // 16 columns: squared norm (column 0)
-constexpr uint32_t kGroupCols = 256;
-constexpr uint32_t kTmemCols = kGroups * kGroupCols;
-constexpr uint32_t kWaitLimit = 1u << 22;           // polls before a wait is declared failed
+constexpr int kStreamsTc = 4;
+constexpr int kASlots = 2, kDSlots = 4;
+constexpr uint32_t kColA = 0;                         // A slot a: columns 128 a .. 128 a + 127
+constexpr uint32_t kColA2 = 64;
+constexpr uint32_t kColD = 256;                       // D slot d: columns 256 + 64 d
+constexpr uint32_t kColD2 = 32;                       // inside a D slot
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kWaitLimit = 1u << 24;             // polls before a wait is declared failed
+constexpr int kLutCopies = 16;
+constexpr int kRowStride = 272;                       // staging row: 256 B + 16 B padding (conflict free)
+constexpr int kStageBytes = 32 * kRowStride + 32 * 32;
 
 // shared memory map (offsets from a 1024-byte aligned base)
-constexpr int kSmQ = 0;            // 32 rows x 256 B, SW128 K-major (two 4 KB atoms)
-constexpr int kSmOnes = 8192;      // 16 rows x 256 B of fp16 1.0
-constexpr int kSmLut = 12288;      // [256 bytes][32 lanes] uint2: byte -> 4 fp16 bucket weights
-constexpr int kSmBar = kSmLut + 256 * 32 * 8;   // kGroups mbarriers
-constexpr int kSmTmem = kSmBar + 8 * kGroups;
+constexpr int kSmQ = 0;                                       // 32 rows x 256 B, SW128 K-major
+constexpr int kSmOnes = 8192;                                 // 16 rows x 256 B of fp16 1.0
+constexpr int kSmStage = 12288;                               // [8 decoders][2] staging buffers
+constexpr int kSmLut = kSmStage + kDecWarps * 2 * kStageBytes;       // [256][16] uint2
+constexpr int kSmMetaT = kSmLut + 256 * kLutCopies * 8;       // [256] int64 first token
+constexpr int kSmMetaL = kSmMetaT + kTcCandPerCta * 8;        // [256] int32 length (<= 0: no work)
+constexpr int kSmTab = kSmMetaL + kTcCandPerCta * 4;          // rbm [256], decomp [1024], bw [4] fp16
+constexpr int kSmChunks = kSmTab + 256 + 1024 + 16;           // [4] chunks per stream
+constexpr int kSmBar = kSmChunks + 16;                        // afull[2] aempty[2] dfull[4] dempty[4]
+constexpr int kNumBars = 2 * kASlots + 2 * kDSlots;
+constexpr int kSmTmem = kSmBar + 8 * kNumBars;
 constexpr int kSmAbort = kSmTmem + 4;
 constexpr int kSmBytes = kSmAbort + 4;
-constexpr int kSmDynamic = 1024 + 150 * 1024;       // > half an SM: one CTA per SM (it holds all 512 TMEM columns)
+constexpr int kSmDynamic = kSmBytes + 1024;
 
 __device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
     __half2 r = __hadd2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
@@ -60,12 +69,11 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a) {
     return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// A stream's position: candidate `ci` (index within the CTA's range), token offset `pos`.
+// A stream's position: candidate `ci` (kTcCandPerCta once exhausted), token offset `pos`.
 struct Cursor {
     int ci;
     int pos;
     int L;
-    int64_t slot;
     int64_t tstart;
 };
 
@@ -75,17 +83,44 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
     extern __shared__ uint8_t s4_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)s4_raw + 1023) & ~(uintptr_t)1023);
     uint2* lut = reinterpret_cast<uint2*>(sm + kSmLut);
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + kSmBar);
+    int64_t* meta_t = reinterpret_cast<int64_t*>(sm + kSmMetaT);
+    int32_t* meta_l = reinterpret_cast<int32_t*>(sm + kSmMetaL);
+    uint8_t* tab_rbm = sm + kSmTab;
+    uint8_t* tab_dec = tab_rbm + 256;
+    __half* tab_bw = reinterpret_cast<__half*>(tab_dec + 1024);
+    int* s_chunks = reinterpret_cast<int*>(sm + kSmChunks);
+    uint64_t* afull = reinterpret_cast<uint64_t*>(sm + kSmBar);
+    uint64_t* aempty = afull + kASlots;
+    uint64_t* dfull = aempty + kASlots;
+    uint64_t* dempty = dfull + kDSlots;
     uint32_t* tbase_s = reinterpret_cast<uint32_t*>(sm + kSmTmem);
     volatile int* abort = reinterpret_cast<volatile int*>(sm + kSmAbort);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = warp / kGroupWarps, quad = warp % kGroupWarps;   // warp % 4 == its TMEM lane quadrant
-    const int stream = warp;
     const int b = blockIdx.y;
     const int64_t cbase = (int64_t)blockIdx.x * kTcCandPerCta;
 
-    // ---- query tile (SW128 K-major), ones tile, replicated byte LUT, barriers, tensor memory
+    // ---- stage the codec tables and the candidates' metadata; trivial outputs
+    for (int i = tid; i < 256; i += kTcThreads) tab_rbm[i] = D.rbm[i];
+    for (int i = tid; i < 1024; i += kTcThreads) tab_dec[i] = D.decomp[i];
+    if (tid < 4) tab_bw[tid] = D.bw[tid];
+    for (int ci = tid; ci < kTcCandPerCta; ci += kTcThreads) {
+        int L = -1;
+        int64_t ts = 0;
+        if (cbase + ci < n) {
+            const int64_t slot = (int64_t)b * n + cbase + ci;
+            const int32_t pid = pids[slot];
+            if (pid < 0 || pid >= D.N) {
+                out[slot] = -INFINITY;
+            } else {
+                L = D.doc_lens[pid];
+                ts = D.doc_offsets[pid];
+                if (L <= 0) out[slot] = -3.2e10f;    // 32 rows x the -1e9 running-max start
+            }
+        }
+        meta_t[ci] = ts;
+        meta_l[ci] = L;
+    }
     const __half* Qb = Q + (int64_t)b * kRows * kDim;
     for (int i = tid; i < kRows * 16; i += kTcThreads) {
         const int row = i >> 4, c16 = i & 15;
@@ -94,16 +129,15 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
     }
     for (int i = tid; i < 256; i += kTcThreads)
         reinterpret_cast<uint4*>(sm + kSmOnes)[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
-    for (int i = tid; i < 256 * 32; i += kTcThreads) {
-        const int byte = i >> 5;                     // one copy per lane: no bank conflicts
-        const int rev = D.rbm[byte];
-        __half wv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) wv[u] = D.bw[D.decomp[rev * 4 + u] & 3];
-        lut[i] = *reinterpret_cast<uint2*>(wv);
-    }
     if (tid == 0) {
-        for (int i = 0; i < kGroups; ++i) tc::mbar_init(mbar + i, 1);
+        for (int i = 0; i < kASlots; ++i) {
+            tc::mbar_init(afull + i, 4);
+            tc::mbar_init(aempty + i, 1);
+        }
+        for (int i = 0; i < kDSlots; ++i) {
+            tc::mbar_init(dfull + i, 1);
+            tc::mbar_init(dempty + i, 4);
+        }
         *abort = 0;
         tc::mbar_fence_init();
     }
@@ -111,167 +145,228 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
         tc::tmem_alloc(tbase_s, kTmemCols);
         tc::tmem_relinquish();
     }
+    __syncthreads();
+    for (int i = tid; i < 256 * kLutCopies; i += kTcThreads) {
+        const int byte = i / kLutCopies;
+        const int rev = tab_rbm[byte];
+        __half wv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) wv[u] = tab_bw[tab_dec[rev * 4 + u] & 3];
+        lut[i] = *reinterpret_cast<uint2*>(wv);
+    }
+    if (warp < kStreamsTc) {                 // chunks per stream (warp q sums stream q)
+        int c = 0;
+        for (int ci = warp + kStreamsTc * lane; ci < kTcCandPerCta; ci += kStreamsTc * 32) {
+            const int L = meta_l[ci];
+            c += L > 0 ? (L + 31) >> 5 : 0;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+        if (lane == 0) s_chunks[warp] = c;
+    }
     tc::fence_proxy_async();
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
-    const uint32_t tbase = *tbase_s + (uint32_t)(g * kGroupCols);
-    const uint32_t tq = tbase + ((uint32_t)(32 * quad) << 16);      // this warp's lane quadrant
-    const uint32_t sQ = tc::smem_u32(sm + kSmQ), sOnes = tc::smem_u32(sm + kSmOnes);
-    constexpr uint32_t idD = tc::idesc_f16_f32(128, 32);
-    constexpr uint32_t idD2 = tc::idesc_f16_f32(128, 16);
-    const int bar_id = 1 + g, bar_n = kGroupWarps * 32;
+    const uint32_t tbase = *tbase_s;
+    const int n_tiles = max(max(s_chunks[0], s_chunks[1]), max(s_chunks[2], s_chunks[3]));
+    bool bad_code = false, failed = false;
 
-    // outputs of candidates that need no MMA (padding / out of range / no tokens)
-    if (lane == 0) {
-        for (int ci = stream; ci < kTcCandPerCta && cbase + ci < n; ci += kStreams) {
-            const int64_t slot = (int64_t)b * n + cbase + ci;
-            const int32_t pid = pids[slot];
-            if (pid < 0 || pid >= D.N) out[slot] = -INFINITY;
-            else if (D.doc_lens[pid] <= 0) out[slot] = -3.2e10f;    // 32 rows x the -1e9 running-max start
-        }
-    }
-    // ---- cursors over this warp's candidates (cbase + stream + k * kStreams), 32 tokens a step
-    auto advance = [&](Cursor& c) {
+    // stream q, chunk by chunk (step = chunks to skip per call)
+    auto advance = [&](Cursor& c, int q) {
         c.pos += 32;
-        if (c.slot >= 0 && c.pos < c.L) return;
+        if (c.ci >= 0 && c.ci < kTcCandPerCta && c.pos < c.L) return;
         for (;;) {
-            c.ci = (c.slot < 0 && c.ci < 0) ? stream : c.ci + kStreams;
+            c.ci = c.ci < 0 ? q : c.ci + kStreamsTc;
             c.pos = 0;
-            if (c.ci >= kTcCandPerCta || cbase + c.ci >= n) {
+            if (c.ci >= kTcCandPerCta) {
                 c.ci = kTcCandPerCta;
-                c.slot = -2;                          // exhausted
                 c.L = 0;
                 return;
             }
-            c.slot = (int64_t)b * n + cbase + c.ci;
-            const int32_t pid = pids[c.slot];
-            if (pid < 0 || pid >= D.N) continue;
-            const int L = D.doc_lens[pid];
+            const int L = meta_l[c.ci];
             if (L <= 0) continue;
             c.L = L;
-            c.tstart = D.doc_offsets[pid];
+            c.tstart = meta_t[c.ci];
             return;
         }
     };
-    auto tok_valid = [&](const Cursor& c) { return c.slot >= 0 && c.pos + lane < c.L; };
 
-    Cursor cc{-1, -32, 0, -1, 0};
-    advance(cc);                 // chunk computed in this iteration
-    Cursor fc = cc;              // chunk whose centroid rows / residuals are in flight
-    Cursor kc = cc;              // chunk whose code is in flight
-    advance(kc);
-
-    uint4 cv[16], r0 = make_uint4(0, 0, 0, 0), r1 = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) cv[j] = make_uint4(0, 0, 0, 0);
-    auto fetch_rows = [&](const Cursor& c, int code) {
-        if (tok_valid(c)) {
-            const int64_t tok = c.tstart + c.pos + lane;
-            const uint4* cr = reinterpret_cast<const uint4*>(D.centroids + (int64_t)code * kDim);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) cv[j] = __ldg(cr + j);
-            r0 = *reinterpret_cast<const uint4*>(D.residuals + tok * 32);
-            r1 = *reinterpret_cast<const uint4*>(D.residuals + tok * 32 + 16);
-        }
-    };
-    {
-        const int code_f = tok_valid(fc) ? D.codes[fc.tstart + fc.pos + lane] : 0;
-        fetch_rows(fc, code_f);
-    }
-    int code_k = tok_valid(kc) ? D.codes[kc.tstart + kc.pos + lane] : 0;
-
-    float run_max = -1e9f;
-    uint32_t phase = 0;
-    bool failed = false;
-    for (;;) {
-        const bool have = cc.slot >= 0;
-        // ---- decode chunk cc from the registers fetched one iteration ago
-        if (have) {
-            const bool valid = tok_valid(cc);
-            uint32_t a[64];
-            if (valid) {
-                const uint32_t rw[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {             // 8 dims = 2 residual bytes per step
-                    const uint32_t word = rw[c >> 1];
-                    const uint32_t by0 = (word >> ((c & 1) * 16)) & 0xFFu;
-                    const uint32_t by1 = (word >> ((c & 1) * 16 + 8)) & 0xFFu;
-                    const uint2 w0 = lut[by0 * 32 + lane], w1 = lut[by1 * 32 + lane];
-                    a[4 * c + 0] = hadd2_u32(cv[c].x, w0.x);
-                    a[4 * c + 1] = hadd2_u32(cv[c].y, w0.y);
-                    a[4 * c + 2] = hadd2_u32(cv[c].z, w1.x);
-                    a[4 * c + 3] = hadd2_u32(cv[c].w, w1.y);
+    if (warp < kDecWarps) {
+        // ================================================================ decoders
+        const int q = warp & 3, par = warp >> 2;
+        const uint32_t tq = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)(par * 128);   // A slot = par
+        uint8_t* stg = sm + kSmStage + warp * 2 * kStageBytes;
+        auto load_code = [&](const Cursor& c) {
+            int code = (c.ci < kTcCandPerCta && c.pos + lane < c.L) ? D.codes[c.tstart + c.pos + lane] : 0;
+            if ((unsigned)code >= (unsigned)D.NC) { bad_code = true; code = 0; }
+            return code;
+        };
+        // coalesced cp.async of chunk c into staging buffer bf (one commit group, maybe empty)
+        auto issue = [&](const Cursor& c, int code_c, int bf) {
+            if (c.ci < kTcCandPerCta) {
+                const int ntv = min(32, c.L - c.pos);
+                uint8_t* dst = stg + bf * kStageBytes;
+                const int hh = lane >> 4, l16 = lane & 15;
+#pragma unroll 4
+                for (int i = 0; i < 16; ++i) {
+                    const int t = 2 * i + hh;
+                    const int code = __shfl_sync(0xFFFFFFFFu, code_c, t);
+                    if (t < ntv)
+                        tc::cp_async16(dst + t * kRowStride + l16 * 16, D.centroids + (int64_t)code * kDim + l16 * 8);
                 }
-            } else {
+                const uint8_t* res = D.residuals + (c.tstart + c.pos) * 32;
+                uint8_t* rdst = dst + 32 * kRowStride;
 #pragma unroll
-                for (int c = 0; c < 64; ++c) a[c] = 0u;
+                for (int j = 0; j < 2; ++j) {
+                    const int off = (j * 32 + lane) * 16;             // 64 pieces of 16 B = 32 tokens
+                    if ((off >> 5) < ntv) tc::cp_async16(rdst + off, res + off);
+                }
             }
-            // ---- issue the next chunk's gathers (their latency overlaps this chunk's MMA/epilogue)
-            fc = kc;
-            fetch_rows(fc, code_k);
-            advance(kc);
-            code_k = tok_valid(kc) ? D.codes[kc.tstart + kc.pos + lane] : 0;
-            tc::st32x32(tq + kColA, *reinterpret_cast<uint32_t(*)[32]>(&a[0]));
-            tc::st32x32(tq + kColA + 32, *reinterpret_cast<uint32_t(*)[32]>(&a[32]));
-            uint32_t a2[32];
-#pragma unroll
-            for (int c = 0; c < 32; ++c) a2[c] = hmul2_u32(a[c]);
-            tc::st32x32(tq + kColA2, a2);
-#pragma unroll
-            for (int c = 0; c < 32; ++c) a2[c] = hmul2_u32(a[32 + c]);
-            tc::st32x32(tq + kColA2 + 32, a2);
-            tc::wait_st();
-        }
-        tc::fence_before();
-        // ---- group barrier: every quadrant written (or the whole group is done)
-        if (!tc::bar_red_or(bar_id, bar_n, have)) break;
-        if (quad == 0 && lane == 0) {
+            tc::cp_async_commit();
+        };
+        Cursor c{-1, -32, 0, 0};
+        advance(c, q);
+        if (par) advance(c, q);
+        int code_c = load_code(c);
+        issue(c, code_c, 0);
+        Cursor cn = c;
+        advance(cn, q);
+        advance(cn, q);
+        int code_n = load_code(cn);
+        int bf = 0;
+        for (int k = par; k < n_tiles; k += 2) {
+            issue(cn, code_n, bf ^ 1);
+            Cursor cnn = cn;
+            advance(cnn, q);
+            advance(cnn, q);
+            const int code_nn = load_code(cnn);
+            tc::cp_async_wait<1>();
+            __syncwarp();
+            // the MMA of this slot's previous tile (k - 2) has finished reading A
+            if (k >= 2 && !tc::mbar_wait_or_abort(aempty + par, ((k - 2) >> 1) & 1, abort, kWaitLimit)) {
+                failed = true;
+                break;
+            }
             tc::fence_after();
+            if (c.ci < kTcCandPerCta) {
+                const bool valid = c.pos + lane < c.L;
+                const uint8_t* row = stg + bf * kStageBytes + lane * kRowStride;
+                const uint8_t* rsd = stg + bf * kStageBytes + 32 * kRowStride + lane * 32;
+                const int lc = lane & (kLutCopies - 1);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t koff = (uint32_t)((k >> 2) * (kRows * 128) + (k & 3) * 32);
-                tc::mma_ts(tbase + kColD, tbase + kColA + 8 * k, tc::sw128_kmajor_desc(sQ + koff), idD, k > 0);
-            }
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t a[32];
+                    const uint4 rr = *reinterpret_cast<const uint4*>(rsd + half * 16);
+                    const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t koff = (uint32_t)((k >> 2) * (16 * 128) + (k & 3) * 32);
-                tc::mma_ts(tbase + kColD2, tbase + kColA2 + 8 * k, tc::sw128_kmajor_desc(sOnes + koff), idD2, k > 0);
+                    for (int cc = 0; cc < 8; ++cc) {        // 8 dims = 2 residual bytes per step
+                        const uint4 cv = *reinterpret_cast<const uint4*>(row + (half * 8 + cc) * 16);
+                        const uint32_t word = rw[cc >> 1];
+                        const uint32_t by0 = (word >> ((cc & 1) * 16)) & 0xFFu;
+                        const uint32_t by1 = (word >> ((cc & 1) * 16 + 8)) & 0xFFu;
+                        const uint2 w0 = lut[by0 * kLutCopies + lc], w1 = lut[by1 * kLutCopies + lc];
+                        a[4 * cc + 0] = hadd2_u32(cv.x, w0.x);
+                        a[4 * cc + 1] = hadd2_u32(cv.y, w0.y);
+                        a[4 * cc + 2] = hadd2_u32(cv.z, w1.x);
+                        a[4 * cc + 3] = hadd2_u32(cv.w, w1.y);
+                    }
+                    if (!valid) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) a[j] = 0u;
+                    }
+                    tc::st32x32(tq + kColA + half * 32, a);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) a[j] = hmul2_u32(a[j]);
+                    tc::st32x32(tq + kColA2 + half * 32, a);
+                }
+                tc::wait_st();
             }
-            tc::mma_commit(mbar + g);
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(afull + par);
+            c = cn;
+            cn = cnn;
+            code_n = code_nn;
+            bf ^= 1;
         }
-        const bool ok = tc::mbar_wait_or_abort(mbar + g, phase, abort, kWaitLimit);
-        if (!tc::bar_red_and(bar_id, bar_n, ok)) { failed = true; break; }
-        phase ^= 1u;
-        tc::fence_after();
-        if (have) {
-            // ---- epilogue: this warp's quadrant = its 32 tokens x 32 query rows
+        tc::cp_async_wait<0>();                 // no copy may land after the CTA exits
+    } else if (warp == kMmaWarp) {
+        // ================================================================ MMA issuer
+        if (lane == 0) {
+            const uint32_t sQ = tc::smem_u32(sm + kSmQ), sOnes = tc::smem_u32(sm + kSmOnes);
+            constexpr uint32_t idD = tc::idesc_f16_f32(128, 32);
+            constexpr uint32_t idD2 = tc::idesc_f16_f32(128, 16);
+            int issued = 0;
+            for (int k = 0; k < n_tiles; ++k) {
+                const int a = k & 1, d = k & 3;
+                if (!tc::mbar_wait_or_abort(afull + a, (k >> 1) & 1, abort, kWaitLimit)) { failed = true; break; }
+                if (k >= kDSlots && !tc::mbar_wait_or_abort(dempty + d, ((k >> 2) - 1) & 1, abort, kWaitLimit)) {
+                    failed = true;
+                    break;
+                }
+                tc::fence_after();
+                const uint32_t ta = tbase + kColA + (uint32_t)(a * 128), td = tbase + kColD + (uint32_t)(d * 64);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t koff = (uint32_t)((kk >> 2) * (kRows * 128) + (kk & 3) * 32);
+                    tc::mma_ts(td, ta + 8 * kk, tc::sw128_kmajor_desc(sQ + koff), idD, kk > 0);
+                }
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t koff = (uint32_t)((kk >> 2) * (16 * 128) + (kk & 3) * 32);
+                    tc::mma_ts(td + kColD2, ta + kColA2 + 8 * kk, tc::sw128_kmajor_desc(sOnes + koff), idD2, kk > 0);
+                }
+                tc::mma_commit(aempty + a);
+                tc::mma_commit(dfull + d);
+                issued = k + 1;
+            }
+            if (failed && issued > 0)                // let the last MMAs finish before memory is freed
+                (void)tc::mbar_wait_bounded(dfull + ((issued - 1) & 3), ((issued - 1) >> 2) & 1, kWaitLimit);
+        }
+        __syncwarp();
+    } else {
+        // ================================================================ epilogue
+        const int q = warp & 3;                  // warps 9..12 -> quadrants 1, 2, 3, 0
+        Cursor e{-1, -32, 0, 0};
+        advance(e, q);
+        float run_max = -1e9f;
+        for (int k = 0; k < n_tiles; ++k) {
+            const int d = k & 3;
+            if (!tc::mbar_wait_or_abort(dfull + d, (k >> 2) & 1, abort, kWaitLimit)) { failed = true; break; }
+            tc::fence_after();
+            const uint32_t td = tbase + kColD + (uint32_t)(d * 64) + ((uint32_t)(32 * q) << 16);
             uint32_t acc[32];
-            tc::ld32x32(tq + kColD, acc);
-            const uint32_t ssb = tc::ld32x1(tq + kColD2);
+            tc::ld32x32(td, acc);
+            const uint32_t ssb = tc::ld32x1(td + kColD2);
             tc::wait_ld();
-            const bool valid = tok_valid(cc);
-            const float inv = rsqrtf(__uint_as_float(ssb) + 1e-12f);
-            float mine = -INFINITY;
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(dempty + d);
+            if (e.ci < kTcCandPerCta) {
+                const bool valid = e.pos + lane < e.L;
+                const float inv = rsqrtf(__uint_as_float(ssb) + 1e-12f);
+                float mine = -INFINITY;
 #pragma unroll
-            for (int r = 0; r < 32; ++r) {
-                const float v = valid ? __uint_as_float(acc[r]) * inv : -INFINITY;
-                const float mx = tc::warp_max_f32(v);
-                mine = (lane == r) ? mx : mine;
-            }
-            run_max = fmaxf(run_max, mine);
-            if (cc.pos + 32 >= cc.L) {
-                float s = run_max;
+                for (int r = 0; r < 32; ++r) {
+                    const float v = valid ? __uint_as_float(acc[r]) * inv : -INFINITY;
+                    const float mx = tc::warp_max_f32(v);
+                    mine = (lane == r) ? mx : mine;
+                }
+                run_max = fmaxf(run_max, mine);
+                if (e.pos + 32 >= e.L) {
+                    float s_ = run_max;
 #pragma unroll
-                for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-                if (lane == 0) out[cc.slot] = s;
-                run_max = -1e9f;
+                    for (int o = 16; o; o >>= 1) s_ += __shfl_xor_sync(0xFFFFFFFFu, s_, o);
+                    if (lane == 0) out[(int64_t)b * n + cbase + e.ci] = s_;
+                    run_max = -1e9f;
+                }
             }
-            advance(cc);
+            advance(e, q);
         }
-        tc::fence_before();
     }
-    if (failed && quad == 0 && lane == 0) atomicExch(err, 1);   // either group may have failed
+    if (failed && lane == 0) atomicExch(err, 1);
+    if (__any_sync(0xFFFFFFFFu, bad_code) && lane == 0) atomicExch(err, 2);
     __syncthreads();
     if (warp == 0) {
         tc::fence_after();
