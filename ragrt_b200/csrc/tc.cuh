@@ -132,6 +132,10 @@ __device__ __forceinline__ void st32x32(uint32_t taddr, const uint32_t (&r)[32])
         : "memory");
 }
 
+__device__ __forceinline__ void st32x1(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ float warp_max_f32(float v) {
     float m;
     asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
