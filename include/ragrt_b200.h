@@ -100,8 +100,9 @@ int ragrt_centroid_topk(const void* d_Q, const int32_t* d_ntok, int32_t B, int32
  * 32 MiB device array per device instead of cudaMallocAsync/cudaFreeAsync.
  *   - The first call on a device (with it current) looks up the array's address
  *     (cudaGetSymbolAddress; may load the module): make it before any stream capture.
- *   - A call that needs more than 32 MiB of scratch (about B x rows x 520 bytes on the
- *     tensor-core path at nc = 32, plus 4 bytes per centroid) returns RAGRT_ERR_ARG.
+ *   - A call that needs more than 32 MiB of scratch (on the tensor-core path about
+ *     B x rows x (520 + NC / 64) bytes at nc = 32, plus 4 bytes per centroid: 17 MB for 256
+ *     queries x 32 rows x 65,536 centroids) returns RAGRT_ERR_ARG.
  *   - All calls on a device share the array: calls that overlap on the GPU race.
  * ragrt_centroid_topk_noalloc_error reads (and with reset != 0 clears) the error word that
  * the tensor-core kernel sets when one of its bounded waits gives up (synchronous).

@@ -10,13 +10,13 @@
 //     address with cudaGetSymbolAddress and caches it; that lookup may load this module
 //     on the device.  Make that first call before any stream capture.
 //   * Limit: a call whose scratch would exceed 32 MiB is rejected with RAGRT_ERR_ARG and
-//     launches nothing.  The tensor-core path needs 4 (NC + 1) bytes of centroid norms plus
-//     8 B x rows x (nslices x (kk + 31) + 1) of per-row lists: about 8.7 MB for B = 256
-//     queries x 32 rows x 65,536 centroids at nc = 32.
+//     launches nothing.  The tensor-core path needs 4 (NC + 1) bytes of centroid norms plus,
+//     per query row, 8 B x (64 nslices + 1) of candidate lists and 2 B per 128-centroid tile
+//     of pre-pass bounds: about 17 MB for B = 256 queries x 32 rows x 65,536 centroids.
 //   * Sharing: every call on a device uses the same array, which keeps the previous call's
-//     contents; what must start at zero (the centroid-norm maximum and the per-row
-//     admission keys) is cleared by each call on its stream.  Calls whose kernels overlap on
-//     the GPU (different streams, or different host threads) race on the array.
+//     contents; each call clears the centroid-norm maximum and rewrites the per-row
+//     admission keys and tile bounds on its stream before they are read.  Calls whose kernels
+//     overlap on the GPU (different streams, or different host threads) race on the array.
 //   * Errors: a bounded wait that gives up inside the tensor-core kernel sets this entry
 //     point's own error word, read by ragrt_centroid_topk_noalloc_error.
 #include <mutex>

@@ -49,6 +49,7 @@ struct S2TcParams {
     const int32_t* ntok;
     uint64_t* partial;
     unsigned long long* gthr;    // [rows_total] best k-th lower-bound key of the row over all slices
+    uint16_t* tilemax;           // [rows_total][tiles_total] pre-pass: fp16 lower bound of each tile's best score
     int* err;
     int rows_total, rows, NC, kk, tiles_total, tiles_per_slice, nslices, stages;
 };
@@ -164,6 +165,9 @@ __device__ __noinline__ uint64_t s2_compact(uint64_t* lst, int& n, int kk, bool 
     return T;
 }
 
+// kTileMax: the pre-pass.  Same GEMM; the epilogue only records, per row and 128-centroid
+// tile, RN16(max acc - eps), a lower bound of the tile's best fp16 score.
+template <bool kTileMax>
 __global__ void __launch_bounds__(kS2TcThreads, 1)
 s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmC, S2TcParams p) {
     extern __shared__ uint8_t s2_raw[];
@@ -293,11 +297,37 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             tc::fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(acce + b);
+            const int c0 = (t0 + i) * kCN;
+            if constexpr (kTileMax) {
+                if (valid) {
+                    const int ncv = min(kCN, p.NC - c0);            // columns past NC hold zero-filled rows
+                    float m4[4];
+#pragma unroll
+                    for (int ch = 0; ch < 4; ++ch) {
+                        float m16[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float a = (ch * 32 + j < ncv) ? __uint_as_float(v[ch][j]) : -INFINITY;
+                            const float b2 = (ch * 32 + j + 16 < ncv) ? __uint_as_float(v[ch][j + 16]) : -INFINITY;
+                            m16[j] = fmaxf(a, b2);
+                        }
+#pragma unroll
+                        for (int w2 = 8; w2 >= 1; w2 >>= 1)
+#pragma unroll
+                            for (int j = 0; j < w2; ++j) m16[j] = fmaxf(m16[j], m16[j + w2]);
+                        m4[ch] = m16[0];
+                    }
+                    const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+                    uint16_t lo = __half_as_ushort(__float2half_rn(mx - (eps_max + fabsf(mx) * 1.2e-7f + 1e-30f)));
+                    if (lo == 0x8000u) lo = 0;
+                    p.tilemax[(int64_t)grow * p.tiles_total + t0 + i] = lo;
+                }
+                continue;
+            }
             if (g > Te) {
                 Te = g;
                 thr = s2_filter_threshold(Te, eps_max);
             }
-            const int c0 = (t0 + i) * kCN;
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
                 uint32_t cand = 0;
@@ -388,7 +418,7 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             }
         }
         // ---- every valid row: final compaction (sorted, trimmed) and write-out
-        for (int src = 0; src < 32; ++src) {
+        for (int src = 0; src < 32 && !kTileMax; ++src) {
             if (!__shfl_sync(0xFFFFFFFFu, valid, src)) continue;
             int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
             const int grow_s = rb * kQM + quad * 32 + src;
@@ -519,6 +549,30 @@ __global__ void s2_merge_tc(const uint64_t* __restrict__ partial, int nslices, i
     if (m && lane == 0) m[(int64_t)b * rows + t] = imputed ? mt : 0.f;
 }
 
+// Warp per row: the kk-th largest of the row's tile lower bounds (radix select on the
+// order-preserving 16-bit code).  kk distinct tiles hold a centroid scoring at least that, so
+// it lower-bounds the row's kk-th fp16 score; it seeds the row's admission key (id part 0:
+// every centroid with an upper bound of that value or more is admitted).
+__global__ void s2_seed_threshold(const uint16_t* __restrict__ tilemax, int tiles, int rows_total, int kk,
+                                  unsigned long long* __restrict__ gthr) {
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows_total) return;
+    const uint16_t* t = tilemax + row * tiles;
+    uint32_t prefix = 0;
+    if (tiles >= kk) {
+        for (int bit = 15; bit >= 0; --bit) {
+            const uint32_t cand = prefix | (1u << bit);
+            int cnt = 0;
+            for (int i = lane; i < tiles; i += 32) cnt += ord16(t[i]) >= cand ? 1 : 0;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
+            if (cnt >= kk) prefix = cand;
+        }
+    }
+    if (lane == 0) gthr[row] = tiles >= kk ? (unsigned long long)prefix << 32 : 0ull;
+}
+
 // max centroid norm (for the chunk filter's error bound) and, optionally, all norms
 __global__ void s2_centroid_norms(const __half* __restrict__ C, int NC, float* __restrict__ cn,
                                   float* __restrict__ cnmax) {
@@ -591,7 +645,8 @@ void s2_tc_plan(int B, int rows, int NC, int& nslices, int& tiles_per_slice) {
 size_t s2_tc_partial_bytes(int B, int rows, int NC, int kk) {
     int ns, tps;
     s2_tc_plan(B, rows, NC, ns, tps);
-    return sizeof(uint64_t) * (size_t)B * ns * rows * kListCap + sizeof(uint64_t) * (size_t)B * rows + 256;
+    return sizeof(uint64_t) * (size_t)B * ns * rows * kListCap + sizeof(uint64_t) * (size_t)B * rows +
+           sizeof(uint16_t) * (size_t)B * rows * ceil_div(NC, kCN) + 512;
 }
 
 int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __half* C, int NC, const float* cnorm,
@@ -609,12 +664,20 @@ int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __hal
     const size_t smem = s2_tc_smem(kk, stages);
     unsigned long long* gthr = reinterpret_cast<unsigned long long*>(
         partial + (size_t)B * nslices * rows * kListCap);
-    RAGRT_CUDA_TRY(cudaMemsetAsync(gthr, 0, sizeof(uint64_t) * (size_t)B * rows, stream));
-    S2TcParams p{Q, C, cnorm, cnmax, ntok, partial, gthr, err, B * rows, rows, NC, kk, (int)ceil_div(NC, kCN), tps,
+    const int tiles_total = (int)ceil_div(NC, kCN);
+    uint16_t* tilemax = reinterpret_cast<uint16_t*>(gthr + (size_t)B * rows);
+    S2TcParams p{Q, C, cnorm, cnmax, ntok, partial, gthr, tilemax, err, B * rows, rows, NC, kk, tiles_total, tps,
                  nslices, stages};
-    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(nslices, (unsigned)ceil_div((int64_t)B * rows, kQM));
-    s2_tc<<<grid, kS2TcThreads, smem, stream>>>(tmQ, tmC, p);
+    // pre-pass: per-row tile bounds -> seeded admission keys; then the selecting pass
+    s2_tc<true><<<grid, kS2TcThreads, smem, stream>>>(tmQ, tmC, p);
+    RAGRT_LAUNCH_CHECK();
+    s2_seed_threshold<<<(unsigned)ceil_div((int64_t)B * rows * 32, 256), 256, 0, stream>>>(tilemax, tiles_total,
+                                                                                          B * rows, kk, gthr);
+    RAGRT_LAUNCH_CHECK();
+    s2_tc<false><<<grid, kS2TcThreads, smem, stream>>>(tmQ, tmC, p);
     RAGRT_LAUNCH_CHECK();
     const int KX = kListCap;
     const int warps = 4;
