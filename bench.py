@@ -375,11 +375,13 @@ def run_ours(args, cfg, rank, world, local):
     dom = max(("s2_centroid_topk", "s3_aggregate", "s4_maxsim"), key=lambda k: stages[k]["ms"])
     d = stages[dom]
     traffic = None
-    tr = load_traffic().get(dom)
-    if tr and "dram_bytes_per_doc_token" in tr:
-        traffic = tr["dram_bytes_per_doc_token"] * cand_tokens / 1e9       # GB per launch, scaled
+    tr = load_traffic().get(dom) or {}
+    if "dram_bytes_per_doc_token" in tr:                                   # Stage 4: one launch per step
+        traffic = tr["dram_bytes_per_doc_token"] * cand_tokens / 1e9
+    elif "dram_bytes_per_algorithmic_byte" in tr and d.get("algorithmic"):
+        traffic = tr["dram_bytes_per_algorithmic_byte"] * d["algorithmic"]
     roofline = {"bound": d["bound"], "achieved": d["achieved"], "peak": d["peak"], "unit": d["unit"],
-                "frac": d["frac"], "traffic": traffic, "traffic_unit": "GB per launch" if traffic else None,
+                "frac": d["frac"], "traffic": traffic, "traffic_unit": "GB per step (ncu DRAM bytes per unit of work, scaled)" if traffic else None,
                 "algorithmic": d.get("algorithmic"), "kernel": dom, "peak_source": peak_kind,
                 "timing": "CUDA events at stage boundaries inside the timed region, mean over steps"}
 

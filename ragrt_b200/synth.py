@@ -20,6 +20,10 @@ configs name.  Fixed choices (the configs leave them open):
   L2-normalised, fp16.
 * Predicates: bit b of a passage is Bernoulli(p_b) with p = (1%, 10%, 50%) on bits 0-2,
   seed 1; stored uint32 (the reference's predicate dtype).
+* Skewed occupancy (the sharded config): with ``topic_zipf = s`` a topic centre is drawn
+  with probability proportional to rank^-s over a seeded random ranking of the centres, for
+  documents and queries alike, so a few centres' posting lists hold a large share of the
+  corpus.
 
 Everything runs in torch on the CPU (tests) or on the GPU (benchmark scale); each
 centre uses its own generator seeded from (seed, centre), so the output does not depend
@@ -64,6 +68,17 @@ def _gen(seed, salt, device):
     return g
 
 
+def topic_sampler(num_centres, seed, zipf, device):
+    """Draw n topic centres: uniform, or Zipf(zipf) over a seeded ranking of the centres."""
+    if not zipf:
+        return lambda n, g: torch.randint(0, num_centres, (n,), generator=g, device=device)
+    gp = _gen(seed, 23, device)
+    rank_to_centre = torch.randperm(num_centres, generator=gp, device=device)
+    w = torch.arange(1, num_centres + 1, device=device, dtype=torch.float64).pow(-float(zipf))
+    w = (w / w.sum()).float()
+    return lambda n, g: rank_to_centre[torch.multinomial(w, n, replacement=True, generator=g)]
+
+
 def _normalize(x):
     return x / x.norm(dim=-1, keepdim=True).clamp_min(1e-12)
 
@@ -77,12 +92,12 @@ def make_centroids(num_centres=NUM_CENTRES, subs=64, seed=0, device="cpu"):
     return centres, cents.half().contiguous()
 
 
-def make_queries(centres, nq, seed=0, ntok=32, topics=QUERY_TOPICS, device=None):
+def make_queries(centres, nq, seed=0, ntok=32, topics=QUERY_TOPICS, device=None, topic_zipf=None):
     """Q fp16 [nq, ntok, 128], L2-normalised rows."""
     device = device or centres.device
     g = _gen(seed, 11, device)
     C = centres.shape[0]
-    qt = torch.randint(0, C, (nq, topics), generator=g, device=device)
+    qt = topic_sampler(C, 0, topic_zipf, device)(nq * topics, g).view(nq, topics)
     pick = torch.randint(0, topics, (nq, ntok), generator=g, device=device)
     cen = torch.gather(qt, 1, pick)
     x = centres[cen] + TOKEN_SIGMA * torch.randn(nq, ntok, DIM, generator=g, device=device)
@@ -90,7 +105,7 @@ def make_queries(centres, nq, seed=0, ntok=32, topics=QUERY_TOPICS, device=None)
 
 
 def make_corpus(num_docs, centres, centroids, len_range=(60, 180), seed=0, topics=DOC_TOPICS,
-                device=None, sample_tokens=1 << 16):
+                device=None, sample_tokens=1 << 16, topic_zipf=None):
     """Documents drawn from the centres; codes are the exact nearest sub-centroid.
 
     Returns dict(doclens int32 [N], doc_offsets int64 [N+1], codes int32 [T],
@@ -107,7 +122,7 @@ def make_corpus(num_docs, centres, centroids, len_range=(60, 180), seed=0, topic
     offsets = torch.zeros(num_docs + 1, dtype=torch.int64, device=device)
     offsets[1:] = torch.cumsum(doclens, 0)
     T = int(offsets[-1])
-    dtopics = torch.randint(0, C, (num_docs, topics), generator=g, device=device)
+    dtopics = topic_sampler(C, 0, topic_zipf, device)(num_docs * topics, g).view(num_docs, topics)
     pid = torch.repeat_interleave(torch.arange(num_docs, device=device), doclens)
     tpick = torch.randint(0, topics, (T,), generator=g, device=device)
     tok_centre = dtopics[pid, tpick]
