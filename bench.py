@@ -51,6 +51,10 @@ CONFIGS = {
                  k_top=10, masks=(1, 2, 4),
                  desc="cfg3 + predicate filters inside Stage 3 (bits with selectivity 1%, 10%, 50%; "
                       "queries cycle through the three masks)"),
+    "cfg5": dict(num_docs=8_800_000, len_range=(20, 120), centres=4096, subs=64, batch=1024, nc=32, K=4096,
+                 k_top=10, masks=None, zipf=1.1, k_per_shard=True,
+                 desc="sharded weft: 8.8M docs (len U[20,120], mean 70), 262,144 fp16 centroids with Zipf(1.1) "
+                      "topic popularity, batch 1,024 x 32 tokens, nprobe 32, 4,096 candidates per shard, top-10"),
     "small": dict(num_docs=200_000, len_range=(60, 180), centres=1024, subs=64, batch=256, nc=32, K=4096,
                   k_top=10, masks=None, desc="cfg3 at 1/10 of the corpus (quick runs)"),
 }
@@ -170,7 +174,8 @@ def build_workload(cfg, rank, world, seed=0):
     t0 = time.time()
     dev = "cuda"
     centres, cents = synth.make_centroids(num_centres=cfg["centres"], subs=cfg["subs"], seed=seed, device=dev)
-    corp = synth.make_corpus(cfg["num_docs"], centres, cents, len_range=cfg["len_range"], seed=seed, device=dev)
+    corp = synth.make_corpus(cfg["num_docs"], centres, cents, len_range=cfg["len_range"], seed=seed, device=dev,
+                             topic_zipf=cfg.get("zipf"))
     preds = synth.make_predicates(cfg["num_docs"], seed=1, device=dev)
     N = cfg["num_docs"]
     from ragrt_b200.shard import shard_range, slice_docs
@@ -253,7 +258,7 @@ def run_reference(args, cfg, rank, world):
 
 def make_queries(centres, cfg, nbatches, seed):
     from ragrt_b200 import synth
-    Q = synth.make_queries(centres, nbatches * cfg["batch"], seed=1000 + seed)
+    Q = synth.make_queries(centres, nbatches * cfg["batch"], seed=1000 + seed, topic_zipf=cfg.get("zipf"))
     return Q.view(nbatches, cfg["batch"], 32, 128)
 
 
@@ -278,7 +283,7 @@ def run_ours(args, cfg, rank, world, local):
     nb = args.warmup + args.steps
     Q = make_queries(centres, cfg, nb, 0)
     B, nc, k_top = cfg["batch"], cfg["nc"], cfg["k_top"]
-    K = min(int(math.ceil(cfg["K"] / world)), wix.N)
+    K = min(cfg["K"] if cfg.get("k_per_shard") else int(math.ceil(cfg["K"] / world)), wix.N)
     masks = make_masks(cfg, B)
     ids = torch.empty(nb, B, k_top, dtype=torch.int32, device="cuda")
     sc = torch.empty(nb, B, k_top, dtype=torch.float32, device="cuda")

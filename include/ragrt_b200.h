@@ -151,6 +151,19 @@ int ragrt_tile_maxsim(const void* d_Q, const int32_t* d_pids, int32_t B, int32_t
                       const uint8_t* d_decomp_table, float* d_out, int32_t mode, void* stream);
 
 /*
+ * Exact TileMaxSim over uncompressed fp16 doc-token embeddings (the exact-rerank workload):
+ * score(pid) = sum over the 32 query rows of max over the passage's tokens of q_r . d_t, fp32
+ * accumulation, no normalisation; pid < 0 or >= num_passages -> -inf, an empty passage ->
+ * -3.2e10.  The reference scores 2-bit compressed tokens only
+ * (tile_maxsim_fused_decomp.cu:125-229); this is the same pipeline without the decode.
+ *   d_Q [B, 32, 128] fp16; d_pids [B, n]; d_doc_emb [T, 128] fp16 (16-byte aligned);
+ *   d_out [B, n] f32.
+ */
+int ragrt_tile_maxsim_exact(const void* d_Q, const int32_t* d_pids, int32_t B, int32_t n,
+                            const int64_t* d_doc_offsets, const int32_t* d_doc_lens, int32_t num_passages,
+                            const void* d_doc_emb, float* d_out, void* stream);
+
+/*
  * Final filter + top-k per query: a candidate whose pid is < 0 or fails the query's mask
  * scores -inf (ragrt_fused_kernel.cu:621-640), then the k best by (score desc, pid asc)
  * (optix_corr_torch_3d.cpp:603-606).  d_preds [num_preds] may be NULL (no filters); a

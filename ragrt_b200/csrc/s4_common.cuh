@@ -15,10 +15,13 @@ struct S4Docs {
     const uint8_t* decomp;
     int N;
     int NC;           // centroid rows (codes outside [0, NC) are rejected in-kernel); INT32_MAX = unchecked
+    const __half* emb = nullptr;   // raw fp16 doc-token embeddings [T, 128]: exact MaxSim, no decode
 };
 
 int s4_simt_launch(const __half* Q, const int32_t* pids, int B, int n, const S4Docs& D, float* out,
                    cudaStream_t stream);
+// D.emb != nullptr: exact MaxSim over raw fp16 doc-token embeddings (sum_r max_t q_r . d_t,
+// no decompression, no normalisation)
 int s4_tc_launch(const __half* Q, const int32_t* pids, int B, int n, const S4Docs& D, float* out,
                  cudaStream_t stream);
 int final_topk_launch(const int32_t* pids, const float* scores, int B, int n, const uint32_t* preds, int num_preds,

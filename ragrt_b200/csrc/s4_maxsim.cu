@@ -175,3 +175,17 @@ extern "C" int ragrt_tile_maxsim(const void* d_Q, const int32_t* d_pids, int32_t
     if (mode == 1) return s4_tc_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
     return s4_simt_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
 }
+
+extern "C" int ragrt_tile_maxsim_exact(const void* d_Q, const int32_t* d_pids, int32_t B, int32_t n,
+                                       const int64_t* d_doc_offsets, const int32_t* d_doc_lens,
+                                       int32_t num_passages, const void* d_doc_emb, float* d_out, void* stream) {
+    RAGRT_REQUIRE(d_Q && d_doc_offsets && d_doc_lens && d_doc_emb, "null argument");
+    RAGRT_REQUIRE(B >= 1 && n >= 0 && num_passages >= 0, "B >= 1, n >= 0, num_passages >= 0 required");
+    if (n == 0) return RAGRT_OK;
+    RAGRT_REQUIRE(d_pids && d_out, "null argument");
+    RAGRT_REQUIRE(((uintptr_t)d_Q & 15) == 0 && ((uintptr_t)d_doc_emb & 15) == 0,
+                  "Q and the doc embeddings must be 16-byte aligned");
+    S4Docs D{d_doc_offsets, d_doc_lens, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, num_passages, 0,
+             (const __half*)d_doc_emb};
+    return s4_tc_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
+}

@@ -75,6 +75,9 @@ struct Cursor {
     int64_t tstart;
 };
 
+// kRaw: exact MaxSim over raw fp16 embeddings (D.emb): the decoders copy the doc's own rows
+// (no codes, residuals or LUT) and the epilogue does not normalise.
+template <bool kRaw>
 __global__ void __launch_bounds__(kTcThreads, 1)
 s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4Docs D, float* __restrict__ out,
       int* __restrict__ err) {
@@ -99,9 +102,11 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
     const int64_t cbase = (int64_t)blockIdx.x * kTcCandPerCta;
 
     // ---- stage the codec tables and the candidates' metadata; trivial outputs
-    for (int i = tid; i < 256; i += kTcThreads) tab_rbm[i] = D.rbm[i];
-    for (int i = tid; i < 1024; i += kTcThreads) tab_dec[i] = D.decomp[i];
-    if (tid < 4) tab_bw[tid] = D.bw[tid];
+    if constexpr (!kRaw) {
+        for (int i = tid; i < 256; i += kTcThreads) tab_rbm[i] = D.rbm[i];
+        for (int i = tid; i < 1024; i += kTcThreads) tab_dec[i] = D.decomp[i];
+        if (tid < 4) tab_bw[tid] = D.bw[tid];
+    }
     for (int ci = tid; ci < kTcCandPerCta; ci += kTcThreads) {
         int L = -1;
         int64_t ts = 0;
@@ -142,7 +147,7 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
         tc::tmem_relinquish();
     }
     __syncthreads();
-    for (int i = tid; i < 256 * kLutCopies; i += kTcThreads) {
+    for (int i = tid; i < (kRaw ? 0 : 256 * kLutCopies); i += kTcThreads) {
         const int byte = i / kLutCopies;
         const int rev = tab_rbm[byte];
         __half wv[4];
@@ -195,6 +200,7 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
         uint8_t* stg = sm + kSmStage + warp * 2 * kStageBytes;
         // the load is only issued here; its value is checked where it is used
         auto load_code = [&](const Cursor& c) {
+            if constexpr (kRaw) return 0;
             return (c.ci < kTcCandPerCta && c.pos + lane < c.L) ? D.codes[c.tstart + c.pos + lane] : 0;
         };
         // coalesced cp.async of chunk c into staging buffer bf (one commit group, maybe empty)
@@ -206,10 +212,20 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
 #pragma unroll 4
                 for (int i = 0; i < 16; ++i) {
                     const int t = 2 * i + hh;
-                    int code = __shfl_sync(0xFFFFFFFFu, code_c, t);
-                    if ((unsigned)code >= (unsigned)D.NC) { bad_code = true; code = 0; }   // never gather outside C
-                    if (t < ntv)
-                        tc::cp_async16(dst + t * kRowStride + l16 * 16, D.centroids + (int64_t)code * kDim + l16 * 8);
+                    if constexpr (kRaw) {
+                        if (t < ntv)
+                            tc::cp_async16(dst + t * kRowStride + l16 * 16, D.emb + (c.tstart + c.pos + t) * kDim + l16 * 8);
+                    } else {
+                        int code = __shfl_sync(0xFFFFFFFFu, code_c, t);
+                        if ((unsigned)code >= (unsigned)D.NC) { bad_code = true; code = 0; }   // never gather outside C
+                        if (t < ntv)
+                            tc::cp_async16(dst + t * kRowStride + l16 * 16,
+                                           D.centroids + (int64_t)code * kDim + l16 * 8);
+                    }
+                }
+                if constexpr (kRaw) {
+                    tc::cp_async_commit();
+                    return;
                 }
                 const uint8_t* res = D.residuals + (c.tstart + c.pos) * 32;
                 uint8_t* rdst = dst + 32 * kRowStride;
@@ -264,6 +280,13 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
 #pragma unroll
                     for (int cc = 0; cc < 8; ++cc) {        // 8 dims = 2 residual bytes per step
                         const uint4 cv = *reinterpret_cast<const uint4*>(row + (half * 8 + cc) * 16);
+                        if constexpr (kRaw) {
+                            a[4 * cc + 0] = cv.x;
+                            a[4 * cc + 1] = cv.y;
+                            a[4 * cc + 2] = cv.z;
+                            a[4 * cc + 3] = cv.w;
+                            continue;
+                        }
                         const uint32_t word = rw[cc >> 1];
                         const uint32_t by0 = (word >> ((cc & 1) * 16)) & 0xFFu;
                         const uint32_t by1 = (word >> ((cc & 1) * 16 + 8)) & 0xFFu;
@@ -278,10 +301,12 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
                         for (int j = 0; j < 32; ++j) a[j] = 0u;
                     }
                     tc::st32x32(tq + half * 32, a);
+                    if constexpr (!kRaw) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) ss = sq_sum_h2(a[j], ss);
+                        for (int j = 0; j < 32; ++j) ss = sq_sum_h2(a[j], ss);
+                    }
                 }
-                tc::st32x1(tbase + ((uint32_t)(32 * q) << 16) + kColD + (uint32_t)((k & 3) * 64) + kColNorm,
+                if constexpr (!kRaw) tc::st32x1(tbase + ((uint32_t)(32 * q) << 16) + kColD + (uint32_t)((k & 3) * 64) + kColNorm,
                            __float_as_uint(ss));
                 tc::wait_st();
             }
@@ -339,7 +364,7 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
             if (lane == 0) tc::mbar_arrive(dempty + d);
             if (e.ci < kTcCandPerCta) {
                 const bool valid = e.pos + lane < e.L;
-                const float inv = rsqrtf(ssv + 1e-12f);
+                const float inv = kRaw ? 1.0f : rsqrtf(ssv + 1e-12f);
                 float mine = -INFINITY;
 #pragma unroll
                 for (int r = 0; r < 32; ++r) {
@@ -374,9 +399,13 @@ int s4_tc_launch(const __half* Q, const int32_t* pids, int B, int n, const S4Doc
     int* d_err = device_error_flag();
     if (!d_err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
     static_assert(kSmBytes + 1024 <= kSmDynamic, "shared memory map exceeds the allocation");
-    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s4_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmDynamic));
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s4_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmDynamic));
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s4_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmDynamic));
     dim3 grid((unsigned)ceil_div(n, kTcCandPerCta), (unsigned)B);
-    s4_tc<<<grid, kTcThreads, kSmDynamic, stream>>>(Q, pids, n, D, out, d_err);
+    if (D.emb)
+        s4_tc<true><<<grid, kTcThreads, kSmDynamic, stream>>>(Q, pids, n, D, out, d_err);
+    else
+        s4_tc<false><<<grid, kTcThreads, kSmDynamic, stream>>>(Q, pids, n, D, out, d_err);
     RAGRT_LAUNCH_CHECK();
     return RAGRT_OK;
 }

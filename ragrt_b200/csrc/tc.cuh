@@ -165,7 +165,7 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Bulk (non-tensor) copy global -> shared, completion counted in bytes on `bar`.  Both
-// addresses 16-byte aligned, size a multiple of 16.  No multicast.
+// addresses 16-byte aligned, size a multiple of 16; a single destination CTA.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
                      "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))

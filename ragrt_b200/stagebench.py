@@ -8,6 +8,8 @@ Per-stage benchmark of the `weft` kernels on seeded synthetic data (one GPU).
   s4   Stage 4 alone: 4,096 candidates per query drawn uniformly
        without replacement from the corpus (seeded per query), fused 2-bit decompression
        + TileMaxSim, batch B.
+  exact  exact TileMaxSim on uncompressed fp16 passages: 64 queries x
+       1,000 candidates each, 20-180 tokens per candidate.
 Prints one JSON line per stage with the mean time per step (CUDA events on the launching
 stream, after warm-up) and the stage's algorithmic work.  Also the program that the ncu
 captures in profiles/ run.
@@ -20,7 +22,7 @@ import time
 import torch
 
 from . import synth, index_build
-from .weft import WeftIndex, centroid_topk
+from .weft import WeftIndex, centroid_topk, tile_maxsim_exact
 
 
 def timed(fn, steps, warmup):
@@ -38,7 +40,7 @@ def timed(fn, steps, warmup):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--stage", default="all", choices=("s2", "s3", "s4", "all"))
+    ap.add_argument("--stage", default="all", choices=("s2", "s3", "s4", "exact", "all"))
     ap.add_argument("--docs", type=int, default=2_000_000)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--nc", type=int, default=32)
@@ -82,6 +84,17 @@ def main():
             b = 36.0 * toks + 16.0 * cand.numel()
             out.append({"stage": "s4", "ms": ms, "gbs": b / ms / 1e6, "doc_tokens_per_s": toks / ms * 1e3,
                         "tflops": 2.0 * 32 * 128 * toks / ms / 1e9, "doc_tokens": toks, "rerank": a.rerank})
+    if a.stage == "exact":
+        nq, per_q = 64, 1000
+        docs = synth.make_exact_docs(nq * per_q, centres, len_range=(20, 180), seed=0, device=dev)
+        Qx = synth.make_queries(centres, nq, seed=7).reshape(nq, 32, 128).contiguous()
+        pids = torch.arange(nq * per_q, dtype=torch.int32, device=dev).view(nq, per_q).contiguous()
+        ms = timed(lambda: tile_maxsim_exact(Qx, pids, docs["doc_offsets"], docs["doclens"], docs["emb"]),
+                   a.steps, a.warmup)
+        toks = int(docs["doclens"].long().sum())
+        b = 256.0 * toks + 16.0 * pids.numel()
+        out.append({"stage": "exact", "ms": ms, "gbs": b / ms / 1e6, "doc_tokens_per_s": toks / ms * 1e3,
+                    "tflops": 2.0 * 32 * 128 * toks / ms / 1e9, "doc_tokens": toks})
     for o in out:
         print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in o.items()}), flush=True)
 

@@ -183,6 +183,25 @@ def make_corpus(num_docs, centres, centroids, len_range=(60, 180), seed=0, topic
     }
 
 
+def make_exact_docs(num_docs, centres, len_range=(20, 180), seed=0, topics=DOC_TOPICS, device=None):
+    """Uncompressed passages for the exact-rerank workload: token = normalize(centre +
+    TOKEN_SIGMA * g) of one of the passage's topic centres, fp16.  Returns dict(doclens int32
+    [N], doc_offsets int64 [N+1], emb fp16 [T, 128])."""
+    device = device or centres.device
+    C = centres.shape[0]
+    g = _gen(seed, 29, device)
+    lo, hi = len_range
+    doclens = torch.randint(lo, hi + 1, (num_docs,), generator=g, device=device, dtype=torch.int64)
+    offsets = torch.zeros(num_docs + 1, dtype=torch.int64, device=device)
+    offsets[1:] = torch.cumsum(doclens, 0)
+    T = int(offsets[-1])
+    dtopics = torch.randint(0, C, (num_docs, topics), generator=g, device=device)
+    pid = torch.repeat_interleave(torch.arange(num_docs, device=device), doclens)
+    tc = dtopics[pid, torch.randint(0, topics, (T,), generator=g, device=device)]
+    emb = _normalize(centres[tc] + TOKEN_SIGMA * torch.randn(T, DIM, generator=g, device=device)).half()
+    return {"doclens": doclens.to(torch.int32), "doc_offsets": offsets, "emb": emb.contiguous()}
+
+
 def make_predicates(num_docs, selectivities=(0.01, 0.10, 0.50), seed=1, device="cpu"):
     """uint32 [N]: bit b set with probability selectivities[b]."""
     g = _gen(seed, 17, device)

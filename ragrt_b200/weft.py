@@ -60,6 +60,28 @@ def centroid_topk(Q, C_, nc, impute=True, ntok=None, full=False):
     return topc, scores, m, full16
 
 
+def tile_maxsim_exact(Q, pids, doc_offsets, doc_lens, doc_emb):
+    """Exact TileMaxSim over raw fp16 doc-token embeddings.  Q [B, 32, 128] (or [32, 128])
+    fp16, pids [B, n] (or [n]) int32, doc_emb [T, 128] fp16 -> f32 scores [B, n] (or [n])."""
+    _need_cuda(Q, pids, doc_offsets, doc_lens, doc_emb)
+    squeeze = Q.dim() == 2
+    Q = _c(Q, torch.float16)
+    if squeeze:
+        Q = Q[None]
+        pids = pids.reshape(1, -1)
+    if Q.shape[1:] != (32, 128):
+        raise RuntimeError(f"MaxSim kernel reads Q as [32, 128]; got {tuple(Q.shape[1:])}")
+    pids = _c(pids, torch.int32)
+    emb = _c(doc_emb, torch.float16)
+    B, n = pids.shape
+    out = torch.empty(B, n, dtype=torch.float32, device=Q.device)
+    if n:
+        _lib.check(_lib.lib().ragrt_tile_maxsim_exact(_ptr(Q), _ptr(pids), B, n, _ptr(_c(doc_offsets, torch.int64)),
+                                                      _ptr(_c(doc_lens, torch.int32)), doc_lens.shape[0], _ptr(emb),
+                                                      _ptr(out), _stream()))
+    return out[0] if squeeze else out
+
+
 def tile_maxsim(Q, pids, doc_offsets, doc_lens, codes, residuals, centroids, bucket_weights,
                 reversed_bit_map, decomp_table, mode=1):
     """Stage 4.  Q [B, 32, 128] (or [32, 128]) fp16, pids [B, n] (or [n]) int32 -> f32 scores."""
