@@ -11,15 +11,15 @@
 //     decoder issues coalesced 16-byte cp.async copies (a half-warp per 256-byte centroid
 //     row) into a padded shared-memory staging buffer, then decodes its current chunk with
 //     lane = token: d = hadd(centroid, LUT[residual byte]) (16-way replicated byte LUT),
-//     written to tensor memory with tcgen05.st (the decoder's A slot); |d|^2 is summed in fp32
-//     and stored into column 32 of the tile's accumulator slot (lane = token).
-//   * 1 MMA thread: per tile, tcgen05.mma with A from tensor memory, D = A.Q^T (N = 32), into
-//     one of 4 accumulator slots (8 instructions per 128 tokens).
+//     written to tensor memory with tcgen05.st (the decoder's A slot), and d*d (A2).
+//   * 2 MMA threads (one warp each, so both issue streams run in parallel): per tile, with A
+//     from tensor memory, D = A.Q^T (N = 32) and D2 = A2.1 (N = 16; column 0 = |d|^2, fp16
+//     squares summed in fp32) into one of 4 accumulator slots.
 //   * 4 epilogue warps (quadrant q): tcgen05.ld of the chunk's 32 tokens x 32 query rows,
 //     scale by rsqrt(|d|^2 + 1e-12), max over tokens per row (redux.sync.max.f32), running
 //     max per candidate, sum over rows after the candidate's last chunk.
-// mbarriers: afull[2] (decoders -> MMA), aempty[2] (MMA done reading A), dfull[4] (MMA ->
-// epilogue), dempty[4] (epilogue done reading D and the norms; awaited by the decoders).  All waits are bounded; a timeout raises
+// mbarriers: afull[2] (decoders -> MMA), aempty[2] (both MMA streams done reading A), dfull[4]
+// (MMA -> epilogue), dempty[4] (epilogue done reading D; awaited by the MMA threads).  All waits are bounded; a timeout raises
 // the device error flag, every role leaves its loop, copies and MMAs in flight are awaited
 // (bounded) and tensor memory is freed.
 #include "common.cuh"
@@ -29,13 +29,14 @@
 namespace ragrt {
 
 constexpr int kDecWarps = 8;
-constexpr int kMmaWarp = kDecWarps;                   // warp 8
-constexpr int kTcThreads = (kDecWarps + 1 + 4) * 32;  // 416
+constexpr int kMmaWarp = kDecWarps;                   // warps 8 (dots) and 9 (norms)
+constexpr int kTcThreads = (kDecWarps + 2 + 4) * 32;  // 448
 constexpr int kTcCandPerCta = 256;
 constexpr int kStreamsTc = 4;
 constexpr int kASlots = 2, kDSlots = 4;
-constexpr uint32_t kColA = 0;                         // A slot a: columns 64 a .. 64 a + 63
-constexpr uint32_t kColD = 128;                       // D slot d: columns 128 + 64 d: 32 dots, |d|^2
+constexpr uint32_t kColA = 0;                         // A slot a: columns 128 a: A (64), A2 (64)
+constexpr uint32_t kColA2 = 64;                       // inside an A slot
+constexpr uint32_t kColD = 256;                       // D slot d: columns 256 + 64 d: 32 dots, D2 (16)
 constexpr uint32_t kColNorm = 32;                     // inside a D slot
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kWaitLimit = 1u << 24;             // polls before a wait is declared failed
@@ -45,6 +46,7 @@ constexpr int kStageBytes = 32 * kRowStride + 32 * 32;
 
 // shared memory map (offsets from a 1024-byte aligned base)
 constexpr int kSmQ = 0;                                       // 32 rows x 256 B, SW128 K-major
+constexpr int kSmOnes = 8192;                                 // 16 rows x 256 B of fp16 1.0
 constexpr int kSmStage = 12288;                               // [8 decoders][2] staging buffers
 constexpr int kSmLut = kSmStage + kDecWarps * 2 * kStageBytes;       // [256][16] uint2
 constexpr int kSmMetaT = kSmLut + 256 * kLutCopies * 8;       // [256] int64 first token
@@ -62,9 +64,10 @@ __device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
     __half2 r = __hadd2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
     return *reinterpret_cast<uint32_t*>(&r);
 }
-__device__ __forceinline__ float sq_sum_h2(uint32_t a, float acc) {
-    const float2 f = __half22float2(*reinterpret_cast<__half2*>(&a));
-    return fmaf(f.y, f.y, fmaf(f.x, f.x, acc));
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a) {
+    __half2 x = *reinterpret_cast<__half2*>(&a);
+    __half2 r = __hmul2(x, x);
+    return *reinterpret_cast<uint32_t*>(&r);
 }
 
 // A stream's position: candidate `ci` (kTcCandPerCta once exhausted), token offset `pos`.
@@ -124,6 +127,8 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
         meta_t[ci] = ts;
         meta_l[ci] = L;
     }
+    for (int i = tid; i < 256; i += kTcThreads)
+        reinterpret_cast<uint4*>(sm + kSmOnes)[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
     const __half* Qb = Q + (int64_t)b * kRows * kDim;
     for (int i = tid; i < kRows * 16; i += kTcThreads) {
         const int row = i >> 4, c16 = i & 15;
@@ -133,10 +138,10 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
     if (tid == 0) {
         for (int i = 0; i < kASlots; ++i) {
             tc::mbar_init(afull + i, 4);
-            tc::mbar_init(aempty + i, 1);
+            tc::mbar_init(aempty + i, 2);
         }
         for (int i = 0; i < kDSlots; ++i) {
-            tc::mbar_init(dfull + i, 1);
+            tc::mbar_init(dfull + i, 2);
             tc::mbar_init(dempty + i, 4);
         }
         *abort = 0;
@@ -196,7 +201,7 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
     if (warp < kDecWarps) {
         // ================================================================ decoders
         const int q = warp & 3, par = warp >> 2;
-        const uint32_t tq = tbase + ((uint32_t)(32 * q) << 16) + kColA + (uint32_t)(par * 64);   // A slot = par
+        const uint32_t tq = tbase + ((uint32_t)(32 * q) << 16) + kColA + (uint32_t)(par * 128);   // A slot = par
         uint8_t* stg = sm + kSmStage + warp * 2 * kStageBytes;
         // the load is only issued here; its value is checked where it is used
         auto load_code = [&](const Cursor& c) {
@@ -255,13 +260,8 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
             const int code_nn = load_code(cnn);
             tc::cp_async_wait<1>();
             __syncwarp();
-            // the MMA of this slot's previous tile (k - 2) has finished reading A, and the
-            // epilogue of tile k - 4 has released accumulator slot k % 4 (and its norms)
+            // the MMAs of this slot's previous tile (k - 2) have finished reading A
             if (k >= 2 && !tc::mbar_wait_or_abort(aempty + par, ((k - 2) >> 1) & 1, abort, kWaitLimit)) {
-                failed = true;
-                break;
-            }
-            if (k >= kDSlots && !tc::mbar_wait_or_abort(dempty + (k & 3), ((k >> 2) - 1) & 1, abort, kWaitLimit)) {
                 failed = true;
                 break;
             }
@@ -271,7 +271,6 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
                 const uint8_t* row = stg + bf * kStageBytes + lane * kRowStride;
                 const uint8_t* rsd = stg + bf * kStageBytes + 32 * kRowStride + lane * 32;
                 const int lc = lane & (kLutCopies - 1);
-                float ss = 0.f;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     uint32_t a[32];
@@ -303,11 +302,10 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
                     tc::st32x32(tq + half * 32, a);
                     if constexpr (!kRaw) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) ss = sq_sum_h2(a[j], ss);
+                        for (int j = 0; j < 32; ++j) a[j] = hmul2_u32(a[j]);
+                        tc::st32x32(tq + kColA2 + half * 32, a);
                     }
                 }
-                if constexpr (!kRaw) tc::st32x1(tbase + ((uint32_t)(32 * q) << 16) + kColD + (uint32_t)((k & 3) * 64) + kColNorm,
-                           __float_as_uint(ss));
                 tc::wait_st();
             }
             tc::fence_before();
@@ -319,22 +317,38 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
             bf ^= 1;
         }
         tc::cp_async_wait<0>();                 // no copy may land after the CTA exits
-    } else if (warp == kMmaWarp) {
-        // ================================================================ MMA issuer
+    } else if (warp < kMmaWarp + 2) {
+        // ================================================================ MMA issuers
+        // warp 8: D = A.Q^T; warp 9: D2 = A2.1 (|d|^2).  Each commits to aempty and dfull
+        // (count 2 each).  In exact mode (no normalisation) warp 9 only keeps the protocol.
+        const bool norms = warp == kMmaWarp + 1;
         if (lane == 0) {
-            const uint32_t sQ = tc::smem_u32(sm + kSmQ);
+            const uint32_t sQ = tc::smem_u32(sm + kSmQ), sOnes = tc::smem_u32(sm + kSmOnes);
             constexpr uint32_t idD = tc::idesc_f16_f32(128, 32);
+            constexpr uint32_t idD2 = tc::idesc_f16_f32(128, 16);
             int issued = 0;
             for (int k = 0; k < n_tiles; ++k) {
                 const int a = k & 1, d = k & 3;
-                // (the decoders that arrived on afull waited for the release of slot d)
                 if (!tc::mbar_wait_or_abort(afull + a, (k >> 1) & 1, abort, kWaitLimit)) { failed = true; break; }
+                if (k >= kDSlots && !tc::mbar_wait_or_abort(dempty + d, ((k >> 2) - 1) & 1, abort, kWaitLimit)) {
+                    failed = true;
+                    break;
+                }
                 tc::fence_after();
-                const uint32_t ta = tbase + kColA + (uint32_t)(a * 64), td = tbase + kColD + (uint32_t)(d * 64);
+                const uint32_t ta = tbase + kColA + (uint32_t)(a * 128), td = tbase + kColD + (uint32_t)(d * 64);
+                if (!norms) {
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t koff = (uint32_t)((kk >> 2) * (kRows * 128) + (kk & 3) * 32);
-                    tc::mma_ts(td, ta + 8 * kk, tc::sw128_kmajor_desc(sQ + koff), idD, kk > 0);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t koff = (uint32_t)((kk >> 2) * (kRows * 128) + (kk & 3) * 32);
+                        tc::mma_ts(td, ta + 8 * kk, tc::sw128_kmajor_desc(sQ + koff), idD, kk > 0);
+                    }
+                } else if (!kRaw) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t koff = (uint32_t)((kk >> 2) * (16 * 128) + (kk & 3) * 32);
+                        tc::mma_ts(td + kColNorm, ta + kColA2 + 8 * kk, tc::sw128_kmajor_desc(sOnes + koff), idD2,
+                                   kk > 0);
+                    }
                 }
                 tc::mma_commit(aempty + a);
                 tc::mma_commit(dfull + d);
@@ -346,7 +360,7 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
         __syncwarp();
     } else {
         // ================================================================ epilogue
-        const int q = warp & 3;                  // warps 9..12 -> quadrants 1, 2, 3, 0
+        const int q = warp & 3;                  // warps 10..13 -> quadrants 2, 3, 0, 1
         Cursor e{-1, -32, 0, 0};
         advance(e, q);
         float run_max = -1e9f;
