@@ -213,14 +213,23 @@ int ragrt_index_stats(ragrt_index* index, uint64_t* out, int32_t reset);
 const char* ragrt_last_error(void);
 
 /*
- * Device-side failure status of the current device: 1 if a kernel gave up a bounded wait
- * (a tensor-core pipeline stage that never completed) since the last reset, else 0 (<0 on
- * error).  Synchronises with the device's error flag.  reset != 0 clears it.
+ * Device-side failure status of the current device since the last reset: 0 none, 1 a kernel
+ * gave up a bounded wait (a tensor-core pipeline stage that never completed), 2 a code
+ * outside [0, num_centroids) was met (the centroid row was not read), 3 the self-test below;
+ * <0 on error.  Synchronises with the device's error flag.  reset != 0 clears it.
  */
 int ragrt_device_error(int32_t reset);
 
 /* Number of kernels this library has launched in the process (all entry points). */
 uint64_t ragrt_launch_count(void);
+
+/*
+ * Test hook, no counterpart in the reference: launches one warp that waits on an mbarrier
+ * nothing arrives on, with the same bounded polling the pipelined kernels use, so that the
+ * wait gives up after `polls` polls and sets the device error flag to 3 (read it with
+ * ragrt_device_error).  The CUDA context stays usable.
+ */
+int ragrt_selftest_wait_timeout(uint32_t polls, void* stream);
 
 /* Library version string. */
 const char* ragrt_version(void);

@@ -51,6 +51,7 @@ _SIGS = {
     "ragrt_version": (C.c_char_p, []),
     "ragrt_launch_count": (C.c_uint64, []),
     "ragrt_device_error": (I32, [I32]),
+    "ragrt_selftest_wait_timeout": (I32, [C.c_uint32, P]),
 }
 
 _lib = None

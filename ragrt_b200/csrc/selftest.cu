@@ -1,0 +1,31 @@
+// selftest.cu -- exercises the bounded-wait error path that every pipelined kernel uses: one
+// warp waits on an mbarrier that nothing arrives on, gives up after `polls` polls, raises the
+// device error flag (value 3) and returns, leaving the context usable.
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace ragrt {
+
+__global__ void k_wait_timeout(uint32_t polls, int* err) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&bar, 1);
+        tc::mbar_fence_init();
+    }
+    __syncwarp();
+    const bool ok = tc::mbar_wait_bounded(&bar, 0, polls);   // phase 0 never completes
+    if (!__all_sync(0xFFFFFFFFu, ok) && threadIdx.x == 0) atomicExch(err, 3);
+}
+
+}  // namespace ragrt
+
+using namespace ragrt;
+
+extern "C" int ragrt_selftest_wait_timeout(uint32_t polls, void* stream) {
+    RAGRT_REQUIRE(polls >= 1 && polls <= (1u << 24), "polls must be in [1, 2^24]");
+    int* err = device_error_flag();
+    if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
+    k_wait_timeout<<<1, 32, 0, (cudaStream_t)stream>>>(polls, err);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}

@@ -137,9 +137,13 @@ def make_corpus(num_docs, centres, centroids, len_range=(60, 180), seed=0, topic
     inv_rbm = np.argsort(rbm).astype(np.int64)          # rbm[inv_rbm[v]] == v
     inv_rbm_t = torch.from_numpy(inv_rbm).to(device)
 
-    def tokens_of_centre(c):
-        n = counts[c]
-        gc = _gen(seed, 1_000 + c, device)
+    CHUNK = 1 << 22                     # tokens generated at once (popular centres are split)
+
+    def tokens_of_centre(c, i=0):
+        # chunk i of centre c's tokens; chunk 0 uses the centre's own generator, so centres
+        # with at most CHUNK tokens come out as one draw
+        n = min(CHUNK, counts[c] - i * CHUNK)
+        gc = _gen(seed, 1_000 + c, device) if i == 0 else _gen(seed, 10_000_000 + c * 65_536 + i, device)
         x = _normalize(centres[c][None, :] + TOKEN_SIGMA * torch.randn(n, DIM, generator=gc, device=device))
         s = x @ cent32[c].T
         k = s.argmax(dim=1)
@@ -167,14 +171,14 @@ def make_corpus(num_docs, centres, centroids, len_range=(60, 180), seed=0, topic
     cut_d = cut.to(device)
     shifts = torch.tensor([6, 4, 2, 0], device=device)
     for c in range(C):
-        if counts[c] == 0:
-            continue
-        k, r = tokens_of_centre(c)
-        idx = order[starts[c]:starts[c + 1]]
-        codes[idx] = (c * subs + k).to(torch.int32)
-        b = torch.bucketize(r, cut_d).view(-1, 32, 4)                 # bucket per dim
-        v = (b << shifts).sum(-1)                                      # decomp_table row index
-        residuals[idx] = inv_rbm_t[v].to(torch.uint8)
+        for i in range((counts[c] + CHUNK - 1) // CHUNK):
+            k, r = tokens_of_centre(c, i)
+            idx = order[starts[c] + i * CHUNK:starts[c] + i * CHUNK + k.shape[0]]
+            codes[idx] = (c * subs + k).to(torch.int32)
+            b = torch.bucketize(r, cut_d).view(-1, 32, 4)             # bucket per dim
+            v = (b << shifts).sum(-1)                                  # decomp_table row index
+            residuals[idx] = inv_rbm_t[v].to(torch.uint8)
+            del k, r, b, v
     return {
         "doclens": doclens.to(torch.int32), "doc_offsets": offsets, "codes": codes,
         "residuals": residuals, "bucket_weights": bw.half().to(device), "bucket_cutoffs": cut.to(device),

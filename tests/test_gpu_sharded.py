@@ -1,0 +1,118 @@
+"""The sharded configuration's data shape on one GPU: a corpus whose topic popularity is
+Zipf(1.1) (a few centroids' posting lists hold a large share of the postings, split into many
+65,535-capped chunks; here the chunk cap is lowered so lists span dozens of chunks), searched
+whole and as three doc-range shards merged by (score desc, pid asc) -- what bench.py does over
+NCCL.  Both are checked against the CPU restatement (oracle/), the sharded one per shard and
+merged the same way.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from ragrt_b200 import index_build, shard, synth
+from tests.helpers import oracle_index, to_cuda, BIND_KEYS
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-3
+
+
+def _bind(d, ix, sh, cents, corp):
+    out = dict(d)
+    out.update({"csr_row_ptrs": ix["csr_row_ptrs"], "csr_col_eids": ix["csr_col_eids"],
+                "csr_block_sums": ix["csr_block_sums"], "csr_lengths": ix["csr_lengths"],
+                "csr_packed_24": ix["csr_packed_24"], "doc_offsets": sh["doc_offsets"], "doc_lens": sh["doclens"],
+                "codes": sh["codes"], "residuals": sh["residuals"], "doc_predicates": sh["preds"]})
+    return out
+
+
+@pytest.fixture(scope="module")
+def zipf_corpus():
+    centres, cents = synth.make_centroids(num_centres=256, subs=64, seed=3)
+    corp = synth.make_corpus(30_000, centres, cents, seed=3, len_range=(20, 120), topic_zipf=1.1)
+    preds = synth.make_predicates(30_000, seed=1)
+    Q = synth.make_queries(centres, 6, seed=77, topic_zipf=1.1)
+    base = {"centroids": cents, "bucket_weights": corp["bucket_weights"],
+            "reversed_bit_map": corp["reversed_bit_map"], "decomp_table": corp["decomp_table"]}
+    return centres, cents, corp, preds, Q, base
+
+
+def _index(corp, preds, cents, base, lo, hi, max_len):
+    sh = shard.slice_docs(corp["doc_offsets"], corp["doclens"], corp["codes"], corp["residuals"], preds, lo, hi)
+    ix = index_build.plain_ivf_index(sh["codes"], sh["doclens"], cents.shape[0], max_len=max_len)
+    d = _bind(base, ix, sh, cents, corp)
+    return d, ix["E"], sh["pid_base"]
+
+
+def _weft(d, E):
+    from ragrt_b200.weft import WeftIndex
+    g = to_cuda(d)
+    return WeftIndex(*[g[k] for k in BIND_KEYS], num_passages=g["doc_lens"].shape[0],
+                     num_centroids=g["centroids"].shape[0], E=E)
+
+
+def _merge(parts, k_top):
+    """parts: list of (ids [B, k], scores [B, k], pid_base) -> merged (ids, scores) by (score desc, pid asc)."""
+    B = parts[0][0].shape[0]
+    ids = np.full((B, k_top), -1, np.int64)
+    sc = np.full((B, k_top), -np.inf, np.float32)
+    for b in range(B):
+        items = [(float(s[b, j]), int(i[b, j]) + base) for i, s, base in parts for j in range(i.shape[1])
+                 if i[b, j] >= 0]
+        items.sort(key=lambda t: (-t[0], t[1]))
+        for j, (s_, p_) in enumerate(items[:k_top]):
+            ids[b, j], sc[b, j] = p_, s_
+    return ids, sc
+
+
+def _check(ids, sc, oids, osc, score_of):
+    for b in range(ids.shape[0]):
+        fin = np.isfinite(osc[b])
+        rel = np.abs(sc[b][fin] - osc[b][fin]) / np.maximum(np.abs(osc[b][fin]), 1.0)
+        assert rel.max(initial=0) < REL_TOL
+        for i in np.flatnonzero(ids[b] != oids[b]):          # ties within tolerance only
+            assert abs(score_of(b, int(ids[b][i])) - osc[b][i]) <= 2 * REL_TOL * max(abs(osc[b][i]), 1.0)
+
+
+def test_zipf_corpus_many_chunks_matches_oracle(zipf_corpus):
+    centres, cents, corp, preds, Q, base = zipf_corpus
+    N = corp["doclens"].shape[0]
+    d, E, _ = _index(corp, preds, cents, base, 0, N, max_len=128)
+    assert E > 16                                   # lists really are split into many chunks
+    wix, oix = _weft(d, E), oracle_index(d)
+    B = Q.shape[0]
+    ntok = torch.full((B,), 32, dtype=torch.int32)
+    masks = torch.tensor([0, 1, 2, 4, 0, 0], dtype=torch.int32)
+    nc, K, k_top = 32, 1000, 10
+    ids, sc = wix.search(Q.cuda(), nc=nc, K=K, k_top=k_top, ntok=ntok.cuda(), masks=masks.cuda())
+    oids, osc, _ = O.weft_search(oix, Q.numpy(), ntok.numpy(), nc, E, masks.numpy(), K, k_top)
+    _check(ids.cpu().numpy(), sc.cpu().numpy(), oids, osc,
+           lambda b, pid: O.tile_maxsim(oix, Q[b].numpy(), np.array([pid], np.int32))[0])
+
+
+def test_three_shards_merged_match_oracle_shards(zipf_corpus):
+    centres, cents, corp, preds, Q, base = zipf_corpus
+    N = corp["doclens"].shape[0]
+    B = Q.shape[0]
+    ntok = np.full(B, 32, np.int32)
+    nc, K, k_top = 32, 400, 10
+    ours, ref, oixs = [], [], []
+    for r in range(3):
+        lo, hi = shard.shard_range(N, r, 3)
+        d, E, pb = _index(corp, preds, cents, base, lo, hi, max_len=65535)
+        wix, oix = _weft(d, E), oracle_index(d)
+        i, s = wix.search(Q.cuda(), nc=nc, K=K, k_top=k_top)
+        ours.append((i.cpu().numpy(), s.cpu().numpy(), pb))
+        oi, os_, _ = O.weft_search(oix, Q.numpy(), ntok, nc, E, None, K, k_top)
+        ref.append((oi, os_, pb))
+        oixs.append((oix, lo, hi))
+    ids, sc = _merge(ours, k_top)
+    oids, osc = _merge(ref, k_top)
+
+    def score_of(b, pid):
+        for oix, lo, hi in oixs:
+            if lo <= pid < hi:
+                return O.tile_maxsim(oix, Q[b].numpy(), np.array([pid - lo], np.int32))[0]
+        raise AssertionError(pid)
+    _check(ids, sc, oids, osc, score_of)
