@@ -134,6 +134,15 @@ int ragrt_weft_candidates(ragrt_index* index, const int32_t* d_topc, const float
                           void* stream);
 
 /*
+ * Per centroid: postings of all its lists (d_total [NC] int64, may be NULL) and those whose
+ * passage passes the filter (pred & mask) != 0 (d_pass [NC] int64; mask 0 = no filter: all).
+ * The inputs of the reference's filter-aware probing: the empty-centroid set of weft_oracle and
+ * pass_c / tot_c of weft_adapt (src/weft_prep.py:75-170, src/engines.py:434-526), which the
+ * reference derives from its filtered index in Python.
+ */
+int ragrt_centroid_pass_counts(ragrt_index* index, uint32_t mask, int64_t* d_pass, int64_t* d_total, void* stream);
+
+/*
  * Stage 4: fused 2-bit residual decompression + TileMaxSim for B queries with n
  * candidates each.  Replaces launch_tile_maxsim_fused_decomp / native_tile_maxsim_fused_decomp
  * (tile_maxsim_fused_decomp.cu:125-251, optix_corr_torch_3d.cpp:865-883).

@@ -13,6 +13,11 @@ CPU path.
 
 ``imputed_passage_scores`` (the reference's test helper, weft_prep.py:70-72) is kept for
 callers that use it.
+
+Filter-aware probing (the `weft_oracle` / `weft_adapt` engines, weft_prep.py:75-170): the same
+functions with the same arguments and results, their top-k on the Stage-2 kernel.  The per-
+centroid inputs they need (postings passing a filter, all postings; a centroid with no passing
+posting is "empty") come from ``WeftIndex.pass_counts(mask)`` / ``centroid_filter_counts``.
 """
 import torch
 
@@ -51,3 +56,74 @@ def native_prep(Q, C, nc, impute=False, compact=False):
 def imputed_passage_scores(best, found, m):
     """best/found [P, T] per passage and token, m [T] -> imputed sums (weft_prep.py:70-72)."""
     return torch.where(found, best, m[None, :]).sum(1)
+
+
+# ---------------------------------------------------------------- filter-aware probing
+def centroid_filter_counts(index, mask):
+    """(pass_c int64 [NC], tot_c int64 [NC], empty bool [NC], n_ok) for a WeftIndex and a filter."""
+    pass_c, tot_c = index.pass_counts(mask)
+    empty = pass_c == 0
+    return pass_c, tot_c, empty, int((~empty).sum())
+
+
+def _topk_values(Q, C, k):
+    """(vals float32 [ntok, k], idx int64 [ntok, k]): the k best fp16 scores (exact, ties to
+    the lower id), unshifted."""
+    topc, vals, _ = native_prep(Q, C, k, impute=False, compact=True)
+    return vals, topc.long()
+
+
+def compact_centroids(C, empty):
+    """(C_ok [n_ok, d], ids int64 [n_ok]) -- the non-empty centroids (weft_prep.py:128-133);
+    C itself and None when no centroid is empty."""
+    if not bool(empty.any()):
+        return C, None
+    ids = (~empty).nonzero().squeeze(1)
+    return C[ids].contiguous(), ids
+
+
+def oracle_fast_prep(Q, C_ok, ids, nc):
+    """Probe the nc nearest non-empty centroids, impute from the (nc+1)-th (weft_prep.py:136-144).
+    Returns (topc int32 [ntok, nc'], compact shifted scores, raw score of the last probed)."""
+    nc = min(nc, C_ok.shape[0] - 1)
+    topc, scores, m = native_prep(Q, C_ok, nc, impute=True, compact=True)
+    if ids is not None:
+        topc = ids[topc.long()].to(torch.int32).contiguous()
+    return topc, scores, scores[:, -1] + m
+
+
+def oracle_prep(Q, C, nc, empty, n_ok):
+    """Reference form of oracle_fast_prep (weft_prep.py:112-125); also returns depth = mean over
+    tokens of how many centroids (empty or not) score >= the last probed one."""
+    C_ok, ids = compact_centroids(C, empty)
+    topc, scores, last = oracle_fast_prep(Q, C_ok, ids, min(nc, n_ok - 1))
+    return topc, scores, unfiltered_depth(Q, C, last)
+
+
+def unfiltered_depth(Q, C, last):
+    """Mean over tokens of the number of centroids scoring >= `last` (weft_prep.py:147-149)."""
+    _, full, _ = native_prep(Q, C, 1, impute=False, compact=False)
+    return (full >= last.float()[:, None]).sum(1).float().mean()
+
+
+def adaptive_probe(Q, C, nc, ncap, pass_c, tot_c, sel, q=1.0, slack=1.0, stats=None):
+    """weft_adapt's probe depth under a filter (weft_prep.py:75-105), same arguments and result
+    (topc int32 [ntok, nc'], compact shifted scores, nc')."""
+    NC = C.shape[0]
+    nc = min(nc, NC - 1)
+    ncap = min(ncap, NC - 1)
+    vals, idx = _topk_values(Q, C, nc + 1)
+    target = sel * tot_c[idx[:, :nc]].sum(1)
+    short = (pass_c[idx[:, :nc]].sum(1) < slack * target).float().mean()
+    if float(short) <= 1.0 - q + 1e-9:
+        nc2 = nc
+    else:
+        vals, idx = _topk_values(Q, C, ncap + 1)
+        cum = pass_c[idx[:, :ncap]].cumsum(1)
+        need = ((cum < target[:, None]).sum(1) + 1).clamp(nc, ncap).float()
+        nc2 = int(torch.quantile(need, q).ceil()) if q < 1.0 else int(need.max())
+        nc2 = max(nc, min(ncap, nc2))
+    m = vals[:, nc2]
+    if stats is not None:
+        stats["last"] = vals[:, nc2 - 1]
+    return idx[:, :nc2].to(torch.int32).contiguous(), (vals[:, :nc2] - m[:, None]).contiguous(), nc2

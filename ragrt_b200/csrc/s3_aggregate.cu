@@ -384,3 +384,44 @@ extern "C" int ragrt_weft_candidates(ragrt_index* ix, const int32_t* d_topc, con
     return s3_run(ix, d_topc, d_scores, full_scores, d_ntok, B, rows, kc, n_eids, d_masks, K, d_cand_pids,
                   d_cand_sums, d_num_touched, ix->ws.base, ix->ws.bytes, stream);
 }
+
+namespace ragrt {
+
+// warp per centroid: postings of all its lists, and those whose passage passes `mask`
+__global__ void k_centroid_pass_counts(const uint8_t* __restrict__ packed, const uint32_t* __restrict__ preds,
+                                       const int64_t* __restrict__ cstart, const int32_t* __restrict__ clists,
+                                       const int64_t* __restrict__ rp, const int64_t* __restrict__ off, int NC,
+                                       uint32_t mask, int64_t* __restrict__ pass, int64_t* __restrict__ total) {
+    const int c = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (c >= NC) return;
+    const int64_t a = cstart[c];
+    const int64_t b = clists[c] ? off[rp[c] + clists[c]] : a;
+    long long n = 0;
+    if (!mask || !preds) {
+        n = (long long)(b - a) * (lane == 0);
+    } else {
+        for (int64_t i = a + lane; i < b; i += 32) n += (preds[load_pid24(packed, i)] & mask) != 0u;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) n += __shfl_xor_sync(0xFFFFFFFFu, n, o);
+    if (lane == 0) {
+        pass[c] = n;
+        if (total) total[c] = b - a;
+    }
+}
+
+}  // namespace ragrt
+
+extern "C" int ragrt_centroid_pass_counts(ragrt_index* ix, uint32_t mask, int64_t* d_pass, int64_t* d_total,
+                                          void* stream) {
+    RAGRT_REQUIRE(ix && d_pass, "null argument");
+    int rc = check_device(ix);
+    if (rc) return rc;
+    const int NC = ix->d.num_centroids;
+    k_centroid_pass_counts<<<(unsigned)ceil_div((int64_t)NC * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+        ix->d.csr_packed_24, ix->d.doc_predicates, ix->cstart, ix->clists, ix->d.csr_row_ptrs, ix->list_off, NC,
+        mask, d_pass, d_total);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}

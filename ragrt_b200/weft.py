@@ -286,6 +286,16 @@ class WeftIndex:
                                                         _stream()))
         return ids, sc
 
+    def pass_counts(self, mask=0):
+        """(pass int64 [NC], total int64 [NC]): postings per centroid whose passage passes
+        (pred & mask) != 0, and all postings per centroid (mask 0: every posting passes)."""
+        dev = self.centroids.device
+        pc = torch.empty(self.NC, dtype=torch.int64, device=dev)
+        tc = torch.empty(self.NC, dtype=torch.int64, device=dev)
+        _lib.check(_lib.lib().ragrt_centroid_pass_counts(self.handle, int(mask) & 0xFFFFFFFF, _ptr(pc), _ptr(tc),
+                                                         _stream()))
+        return pc, tc
+
     def stats(self, reset=False):
         buf = (C.c_uint64 * _lib.NUM_STATS)()
         _lib.check(_lib.lib().ragrt_index_stats(self.handle, buf, int(bool(reset))))
