@@ -212,6 +212,9 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
         auto issue = [&](const Cursor& c, int code_c, int bf) {
             if (c.ci < kTcCandPerCta) {
                 const int ntv = min(32, c.L - c.pos);
+                if constexpr (!kRaw) {
+                    if ((unsigned)code_c >= (unsigned)D.NC) { bad_code = true; code_c = 0; }   // never gather outside C
+                }
                 uint8_t* dst = stg + bf * kStageBytes;
                 const int hh = lane >> 4, l16 = lane & 15;
 #pragma unroll 4
@@ -221,8 +224,7 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
                         if (t < ntv)
                             tc::cp_async16(dst + t * kRowStride + l16 * 16, D.emb + (c.tstart + c.pos + t) * kDim + l16 * 8);
                     } else {
-                        int code = __shfl_sync(0xFFFFFFFFu, code_c, t);
-                        if ((unsigned)code >= (unsigned)D.NC) { bad_code = true; code = 0; }   // never gather outside C
+                        const int code = __shfl_sync(0xFFFFFFFFu, code_c, t);
                         if (t < ntv)
                             tc::cp_async16(dst + t * kRowStride + l16 * 16,
                                            D.centroids + (int64_t)code * kDim + l16 * 8);
@@ -287,15 +289,15 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
                             continue;
                         }
                         const uint32_t word = rw[cc >> 1];
-                        const uint32_t by0 = (word >> ((cc & 1) * 16)) & 0xFFu;
-                        const uint32_t by1 = (word >> ((cc & 1) * 16 + 8)) & 0xFFu;
+                        const uint32_t by0 = __byte_perm(word, 0u, 0x4440u + (cc & 1) * 2);
+                        const uint32_t by1 = __byte_perm(word, 0u, 0x4441u + (cc & 1) * 2);
                         const uint2 w0 = lut[by0 * kLutCopies + lc], w1 = lut[by1 * kLutCopies + lc];
                         a[4 * cc + 0] = hadd2_u32(cv.x, w0.x);
                         a[4 * cc + 1] = hadd2_u32(cv.y, w0.y);
                         a[4 * cc + 2] = hadd2_u32(cv.z, w1.x);
                         a[4 * cc + 3] = hadd2_u32(cv.w, w1.y);
                     }
-                    if (!valid) {
+                    if (c.pos + 32 > c.L && !valid) {              // only the last chunk of a candidate
 #pragma unroll
                         for (int j = 0; j < 32; ++j) a[j] = 0u;
                     }
@@ -380,11 +382,20 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
                 const bool valid = e.pos + lane < e.L;
                 const float inv = kRaw ? 1.0f : rsqrtf(ssv + 1e-12f);
                 float mine = -INFINITY;
+                const float sc = valid ? inv : 0.f;
+                if (e.pos + 32 <= e.L) {                         // full chunk: no token to mask
 #pragma unroll
-                for (int r = 0; r < 32; ++r) {
-                    const float v = valid ? __uint_as_float(acc[r]) * inv : -INFINITY;
-                    const float mx = tc::warp_max_f32(v);
-                    mine = (lane == r) ? mx : mine;
+                    for (int r = 0; r < 32; ++r) {
+                        const float mx = tc::warp_max_f32(__uint_as_float(acc[r]) * sc);
+                        mine = (lane == r) ? mx : mine;
+                    }
+                } else {
+#pragma unroll
+                    for (int r = 0; r < 32; ++r) {
+                        const float v = valid ? __uint_as_float(acc[r]) * inv : -INFINITY;
+                        const float mx = tc::warp_max_f32(v);
+                        mine = (lane == r) ? mx : mine;
+                    }
                 }
                 run_max = fmaxf(run_max, mine);
                 if (e.pos + 32 >= e.L) {
