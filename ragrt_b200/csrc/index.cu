@@ -204,8 +204,9 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
     ix->d = d;
     cudaGetDevice(&ix->device);
     const int NC = d.num_centroids;
-    // pid range width: 8192 passages unless the range-offset table would exceed 1 GiB
-    int ws = 13;
+    // pid range width: 4096 passages (3 Stage-3 CTAs per SM) unless the range-offset table
+    // would exceed 1 GiB
+    int ws = 12;
     while ((double)NC * (ceil_div(d.num_passages, (int64_t)1 << ws) + 1) * 4.0 > (double)(1ull << 30) && ws < 16)
         ++ws;
     ix->w_shift = ws;

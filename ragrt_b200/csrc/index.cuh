@@ -13,7 +13,7 @@ struct ragrt_index {
     int device = 0;
 
     // pid ranges ("tiles") used by Stage 3: range r holds pids [r << w_shift, (r+1) << w_shift)
-    int w_shift = 13;
+    int w_shift = 12;
     int num_ranges = 0;            // R = ceil(N / W)
 
     int64_t* list_off = nullptr;   // [num_lists + 1] posting offset of every list

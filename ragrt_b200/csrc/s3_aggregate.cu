@@ -62,7 +62,7 @@ __device__ __forceinline__ uint16_t f2h_pos15(float base) {
     return (uint16_t)(__half_as_ushort(__float2half_rn(base)) & 0x7FFF);   // ragrt_fused_kernel.cu:366
 }
 
-__global__ void __launch_bounds__(kS3Threads)
+__global__ void __launch_bounds__(kS3Threads, 3)
 s3_accumulate(S3Params p) {
     extern __shared__ __align__(16) unsigned char s3_smem[];
     const int W = 1 << p.w_shift;
