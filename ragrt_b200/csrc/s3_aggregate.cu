@@ -62,19 +62,18 @@ __device__ __forceinline__ uint16_t f2h_pos15(float base) {
     return (uint16_t)(__half_as_ushort(__float2half_rn(base)) & 0x7FFF);   // ragrt_fused_kernel.cu:366
 }
 
-__global__ void __launch_bounds__(kS3Threads, 3)
+__global__ void __launch_bounds__(kS3Threads, 4)
 s3_accumulate(S3Params p) {
     extern __shared__ __align__(16) unsigned char s3_smem[];
     const int W = 1 << p.w_shift;
     unsigned long long* sums = reinterpret_cast<unsigned long long*>(s3_smem);          // [W]
     uint32_t* seen = reinterpret_cast<uint32_t*>(sums + W);                              // [warps][W/32]
-    uint16_t* touched = reinterpret_cast<uint16_t*>(seen + kS3Warps * (W >> 5));         // [W]
-    int64_t* pcs = reinterpret_cast<int64_t*>(touched + W);                              // [32][kc] cstart
+    int64_t* pcs = reinterpret_cast<int64_t*>(seen + kS3Warps * (W >> 5));               // [32][kc] cstart
     int32_t* pc = reinterpret_cast<int32_t*>(pcs + kRows * p.kc);                        // [32][kc] centroid
     int32_t* pcnt = pc + kRows * p.kc;                                                   // [32][kc] postings
     uint16_t* pv = reinterpret_cast<uint16_t*>(pcnt + kRows * p.kc);                     // [32][kc] fp16 bits
     __shared__ int s_np[kRows];
-    __shared__ unsigned s_ntouched;
+    __shared__ unsigned s_wcnt[kS3Warps];
     __shared__ unsigned s_unit;
     __shared__ unsigned long long s_base;
 
@@ -82,7 +81,6 @@ s3_accumulate(S3Params p) {
     uint32_t* my_seen = seen + w * (W >> 5);
     for (int i = tid; i < W; i += kS3Threads) sums[i] = 0ull;
     for (int i = tid; i < kS3Warps * (W >> 5); i += kS3Threads) seen[i] = 0u;
-    if (tid == 0) s_ntouched = 0;
     unsigned long long st_post = 0, st_probes = 0;
     int cached_q = -1;
     const unsigned total_units = (unsigned)p.nq * (unsigned)p.R;
@@ -204,7 +202,7 @@ s3_accumulate(S3Params p) {
                             if (!(old & bit)) {
                                 const unsigned long long add = (h_fixed24(vb[u]) << 6) | 1ull;
                                 const unsigned long long prev = atomicAdd(&sums[local], add);
-                                if (prev == 0ull) touched[atomicAdd(&s_ntouched, 1u)] = (uint16_t)local;
+                                (void)prev;
                             }
                         }
                     }
@@ -216,20 +214,34 @@ s3_accumulate(S3Params p) {
         }
         __syncthreads();
 
-        // ---- emit touched passages of this tile into the query's pool
-        const unsigned nt_touched = s_ntouched;
-        if (tid == 0 && nt_touched) s_base = atomicAdd(&p.pool_count[qi], (unsigned long long)nt_touched);
+        // ---- emit the tile's touched passages into the query's pool: warp w scans accumulators
+        // [w W/8, (w+1) W/8), counts the non-zero ones, one pool reservation per tile, then
+        // writes their ranking keys and clears them
+        const int seg = W / kS3Warps;
+        const unsigned long long* sw = sums + w * seg;
+        unsigned cnt = 0;
+        for (int i = lane; i < seg; i += 32) cnt += __popc(__ballot_sync(0xFFFFFFFFu, sw[i] != 0ull));
+        if (lane == 0) s_wcnt[w] = cnt;
         __syncthreads();
-        uint64_t* pool = p.pool + (int64_t)qi * p.pool_cap;
-        for (unsigned i = tid; i < nt_touched; i += kS3Threads) {
-            const int local = touched[i];
-            const unsigned long long acc = sums[local];
-            sums[local] = 0ull;
-            const float s = __ull2float_rn(acc >> 6) * 0x1p-24f;
-            pool[s_base + i] = rank_key(s, (int32_t)(range_lo + local));
+        if (tid == 0) {
+            unsigned tot = 0;
+            for (int i = 0; i < kS3Warps; ++i) { const unsigned c = s_wcnt[i]; s_wcnt[i] = tot; tot += c; }
+            s_base = tot ? atomicAdd(&p.pool_count[qi], (unsigned long long)tot) : 0ull;
         }
         __syncthreads();
-        if (tid == 0) s_ntouched = 0;
+        uint64_t* pool = p.pool + (int64_t)qi * p.pool_cap;
+        unsigned long long pos = s_base + s_wcnt[w];
+        for (int i = lane; i < seg; i += 32) {
+            const unsigned long long acc = sums[w * seg + i];
+            const unsigned m = __ballot_sync(0xFFFFFFFFu, acc != 0ull);
+            if (acc) {
+                sums[w * seg + i] = 0ull;
+                const float sc = __ull2float_rn(acc >> 6) * 0x1p-24f;
+                pool[pos + __popc(m & ((1u << lane) - 1u))] = rank_key(sc, (int32_t)(range_lo + w * seg + i));
+            }
+            pos += __popc(m);
+        }
+        __syncthreads();
     }
     // stats: postings scanned (per kept probe, whole list), kept probes
     for (int o = 16; o; o >>= 1) {
@@ -312,7 +324,7 @@ int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_s
     unsigned int* work = (unsigned int*)wsp;
 
     const size_t smem = sizeof(unsigned long long) * W + sizeof(uint32_t) * kS3Warps * (W >> 5) +
-                        sizeof(uint16_t) * W + (sizeof(int64_t) + 2 * sizeof(int32_t) + sizeof(uint16_t)) * kRows * kc + 16;
+                        (sizeof(int64_t) + 2 * sizeof(int32_t) + sizeof(uint16_t)) * kRows * kc + 16;
     if (smem > 220 * 1024) return fail(RAGRT_ERR_CAPACITY, "stage-3 tile needs %zu bytes of shared memory", smem);
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s3_accumulate, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
