@@ -7,9 +7,10 @@
 // (pid, token), sum per pid), optix_corr_torch_3d.cpp:569-585 (top-k candidates).
 //
 // B200 design (no sort, no host synchronisation):
-//   * The pid space is cut into ranges of W = 2^w_shift passages.  A CTA owns one
-//     (query, range) tile and keeps, per passage of the range, a 64-bit accumulator in
-//     shared memory: (sum of fp16 maxima in units of 2^-24) << 6 | (number of tokens).
+//   * The pid space is cut into ranges of W = 2^w_shift passages.  A work item is one query
+//     and 8 consecutive ranges (so the query's probe table is built once per item); for each
+//     range the CTA keeps, per passage, a 64-bit accumulator in shared memory: (sum of fp16
+//     maxima in units of 2^-24) << 6 | (number of tokens).
 //   * A warp processes one query token at a time.  Its probes are sorted by score
 //     (native_prep returns them best first), so the FIRST probe of token t that holds a
 //     passage carries that token's max: a per-warp "seen" bitmap over the range marks
@@ -17,8 +18,9 @@
 //     __match_any_sync in favour of the lowest lane (= the better probe).
 //   * The posting sub-list of centroid c that falls in range r is read directly through
 //     the index's range-offset table (boff), coalesced, once per (token, probe).
-//   * Touched passages are emitted as 64-bit ranking keys into a per-query pool; a
-//     per-query CTA then selects the K candidates exactly (radix select + bitonic sort).
+//   * Touched passages (non-zero accumulators, found by a scan at the end of each range) are
+//     emitted as 64-bit ranking keys into a per-query pool; a per-query CTA then selects the
+//     K candidates exactly (radix select + bitonic sort).
 // Sums are exact (fixed point) and rounded once to fp32; ties in candidate selection go to
 // the lower pid.
 #include <algorithm>
@@ -31,6 +33,7 @@ namespace ragrt {
 
 constexpr int kS3Warps = 8;
 constexpr int kS3Threads = kS3Warps * 32;
+constexpr int kS3RangesPerJob = 8;   // consecutive pid ranges of one query per work item (one probe table)
 constexpr int kS3Batch = 8;       // 32-posting chunks whose pid loads a warp keeps in flight together
 
 struct S3Params {
@@ -83,15 +86,18 @@ s3_accumulate(S3Params p) {
     for (int i = tid; i < kS3Warps * (W >> 5); i += kS3Threads) seen[i] = 0u;
     unsigned long long st_post = 0, st_probes = 0;
     int cached_q = -1;
-    const unsigned total_units = (unsigned)p.nq * (unsigned)p.R;
+    const unsigned nrb = ((unsigned)p.R + kS3RangesPerJob - 1) / kS3RangesPerJob;
+    const unsigned total_jobs = (unsigned)p.nq * nrb;
     __syncthreads();
 
     for (;;) {
         if (tid == 0) s_unit = atomicAdd(p.work, 1u);
         __syncthreads();
-        const unsigned unit = s_unit;
-        if (unit >= total_units) break;
-        const int qi = (int)(unit / p.R), r = (int)(unit % p.R);
+        const unsigned job = s_unit;
+        if (job >= total_jobs) break;
+        const int qi = (int)(job / nrb);
+        const int r0 = (int)(job % nrb) * kS3RangesPerJob, r1 = min(p.R, r0 + kS3RangesPerJob);
+      for (int r = r0; r < r1; ++r) {
         const int q = p.q0 + qi;
         const uint32_t mask = p.masks ? p.masks[q] : 0u;
         const int nt = p.ntok ? min(p.ntok[q], p.rows) : p.rows;
@@ -242,6 +248,7 @@ s3_accumulate(S3Params p) {
             pos += __popc(m);
         }
         __syncthreads();
+      }
     }
     // stats: postings scanned (per kept probe, whole list), kept probes
     for (int o = 16; o; o >>= 1) {
@@ -361,8 +368,8 @@ int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_s
         p.work = work;
         p.stats = ix->stats;
         if (masks && !ix->d.doc_predicates) p.masks = nullptr;   // no predicates bound: no filter
-        const int64_t units = (int64_t)nq * ix->num_ranges;
-        const int grid = (int)std::min<int64_t>(units, (int64_t)per_sm * num_sms());
+        const int64_t jobs = (int64_t)nq * ((ix->num_ranges + kS3RangesPerJob - 1) / kS3RangesPerJob);
+        const int grid = (int)std::min<int64_t>(jobs, (int64_t)per_sm * num_sms());
         s3_accumulate<<<grid, kS3Threads, smem, stream>>>(p);
         RAGRT_LAUNCH_CHECK();
         s3_query_lists<<<nq, 256, 0, stream>>>(p, counts + sub);
