@@ -169,6 +169,10 @@ s3_accumulate(S3Params p) {
                 const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
                 const int excl = incl - len;
                 st_post += (unsigned long long)len;
+                // posting e of the group lives at (start - excl) + e in the probe's list: that base
+                // (signed, 48 bits) and the probe's fp16 value travel in one 64-bit shuffle
+                const unsigned long long bv = ((unsigned long long)v << 48) |
+                                              ((unsigned long long)(start - excl) & 0xFFFFFFFFFFFFull);
                 // kS3Batch chunks of 32 postings at a time: all their pid (and predicate) loads
                 // are issued before the first chunk is merged, in posting order
                 for (int e0 = 0; e0 < total; e0 += 32 * kS3Batch) {
@@ -185,10 +189,10 @@ s3_accumulate(S3Params p) {
                             int ex = __shfl_sync(0xFFFFFFFFu, excl, cand & 31);
                             if (cand < 32 && ex <= e) src = cand;
                         }
-                        const int ex_src = __shfl_sync(0xFFFFFFFFu, excl, src);
-                        const int64_t st_src = __shfl_sync(0xFFFFFFFFu, start, src);
-                        vb[u] = (uint16_t)__shfl_sync(0xFFFFFFFFu, (int)v, src);
-                        pid[u] = e < total ? load_pid24(p.packed, st_src + (e - ex_src)) : -1;
+                        const unsigned long long bv_src = __shfl_sync(0xFFFFFFFFu, bv, src);
+                        vb[u] = (uint16_t)(bv_src >> 48);
+                        const int64_t base = (int64_t)(bv_src << 16) >> 16;
+                        pid[u] = e < total ? load_pid24(p.packed, base + e) : -1;
                     }
                     uint32_t pr[kS3Batch];
 #pragma unroll
