@@ -53,12 +53,18 @@ def build(force=False, jobs=None, verbose=False):
     srcs = _sources()
     with cf.ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, force, verbose), srcs))
-    newest = max(os.path.getmtime(o) for o in objs)
-    if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
+    # Objects are cached by content, so a source put back to an earlier state reuses an older
+    # object: relink whenever the set of objects differs from the one the library was linked from.
+    stamp = os.path.join(OBJ_DIR, "libragrt_b200.objs")
+    linked = open(stamp).read() if os.path.exists(stamp) else ""
+    want = "\n".join(os.path.basename(o) for o in objs)
+    if force or not os.path.exists(LIB) or linked != want:
         cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        with open(stamp, "w") as f:
+            f.write(want)
     return LIB
 
 
