@@ -25,9 +25,11 @@ per-shard top-k lists are merged with one NCCL all-gather.  Whole-job work is fi
 threads) on a bounded sample of the same workload, rank 0 only.
 """
 import argparse
+import datetime
 import json
 import math
 import os
+import shutil
 import subprocess
 import sys
 import threading
@@ -83,8 +85,10 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms, started before the warm-up so
+    that it is running when the timed region begins; `summary` keeps the samples whose own
+    nvidia-smi timestamp lies inside the window set by `mark_start` / `mark_end`."""
+    Q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
@@ -92,11 +96,20 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.out = []
+        self.t0 = self.t1 = None
+
+    def mark_start(self):
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self):
+        self.t1 = datetime.datetime.now()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+            # line-buffered (stdbuf) so that each sample reaches the reader when it is taken
+            pre = ["stdbuf", "-oL"] if shutil.which("stdbuf") else []
+            self.proc = subprocess.Popen(pre + ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -110,6 +123,7 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc:
+            time.sleep(0.2)                      # the samples of the region's last 50 ms
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -124,6 +138,9 @@ class ClockSampler:
             if len(f) < 9:
                 continue
             try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f")
+                if self.t0 is not None and not (self.t0 <= ts <= (self.t1 or ts)):
+                    continue
                 sm.append(float(f[1]))
                 smax = max(smax, float(f[2]))
             except ValueError:
@@ -131,8 +148,10 @@ class ClockSampler:
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
+        window = (self.t1 - self.t0).total_seconds() if self.t0 and self.t1 else None
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "window_s": window,
+                "interval_ms": 50}
 
 
 def dist_setup(n_gpus):
@@ -298,21 +317,23 @@ def run_ours(args, cfg, rank, world, local):
             merge_shards(ids[i], sc[i], world, k_top, shard["pid_base"])
 
     # ---- warm-up, then the timed region (inputs resident in HBM, a new query batch per step)
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    barrier(world)
-    wix.stats(reset=True)
-    l0 = _lib.lib().ragrt_launch_count()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        for i in range(args.warmup):
+            step(i)
         torch.cuda.synchronize()
         barrier(world)
+        wix.stats(reset=True)
+        l0 = _lib.lib().ragrt_launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        barrier(world)
+        clocks.mark_start()
         e0.record(stream)
         for i in range(args.warmup, nb):
             step(i)
         e1.record(stream)
         torch.cuda.synchronize()
+        clocks.mark_end()
         barrier(world)
     launches = _lib.lib().ragrt_launch_count() - l0
     ms = max_over_ranks(e0.elapsed_time(e1), world)
