@@ -16,10 +16,11 @@ is the same through the public API with the query batch copied from pinned host 
 and the results copied back inside every timed step.  `stages` and `roofline` come from a
 second timed pass that records CUDA events at the stage boundaries on the launching stream.
 
-Multi-GPU (--gpus N under torchrun): the corpus is sharded by contiguous pid ranges, every
-rank searches the same query batch against its shard (per-shard K = ceil(K / N)), and the
-per-shard top-k lists are merged with one NCCL all-gather.  Whole-job work is fixed
-("scaling": "strong").
+Multi-GPU (--gpus N under torchrun): the corpus is sharded by contiguous pid ranges.  Each
+rank runs Stage 2 for its slice of the query batch and one NCCL all-gather gives every rank
+the whole batch's probe lists; every rank then runs Stages 1-4 for the whole batch against its
+shard (per-shard K = ceil(K / N)), and the per-shard top-k lists are merged with a second
+all-gather (ragrt_b200.shard.sharded_search).  Whole-job work is fixed ("scaling": "strong").
 
 --impl reference times the CPU restatement of the reference path (oracle/, all host
 threads) on a bounded sample of the same workload, rank 0 only.
@@ -289,10 +290,10 @@ def make_masks(cfg, B):
 
 
 # ----------------------------------------------------------------------------- ours
-def merge_shards(ids, sc, world, k_top, pid_base):
-    """All-gather per-shard top-k (score, global pid) and merge (score desc, pid asc)."""
-    from ragrt_b200.shard import merge_topk
-    return merge_topk(ids, sc, world, k_top, pid_base)
+def sharded_search(*a, **kw):
+    """Stage 2 by query slice + probe all-gather, Stages 1-4 on the doc shard, merged top-k."""
+    from ragrt_b200.shard import sharded_search as ss
+    return ss(*a, **kw)
 
 
 def run_ours(args, cfg, rank, world, local):
@@ -312,9 +313,11 @@ def run_ours(args, cfg, rank, world, local):
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(nb)]
 
     def step(i):
-        wix.search_profiled(Q[i], ev[i], nc=nc, K=K, k_top=k_top, masks=masks, out=(ids[i], sc[i]))
-        if world > 1:
-            merge_shards(ids[i], sc[i], world, k_top, shard["pid_base"])
+        if world == 1:
+            wix.search_profiled(Q[i], ev[i], nc=nc, K=K, k_top=k_top, masks=masks, out=(ids[i], sc[i]))
+        else:                # Stage 2 split over the ranks by query, the rest on this rank's doc shard
+            sharded_search(wix, Q[i], world, rank, shard["pid_base"], nc=nc, K=K, k_top=k_top, masks=masks,
+                           events=ev[i])
 
     # ---- warm-up, then the timed region (inputs resident in HBM, a new query batch per step)
     with ClockSampler(local) as clocks:
@@ -351,9 +354,11 @@ def run_ours(args, cfg, rank, world, local):
     e2.record(stream)
     for i in range(args.warmup, nb):
         Qd.copy_(Qh[i], non_blocking=True)
-        o_ids, o_sc = wix.search(Qd, nc=nc, K=K, k_top=k_top, masks=masks)
-        if world > 1:
-            o_ids, o_sc = merge_shards(o_ids, o_sc, world, k_top, shard["pid_base"])
+        if world == 1:
+            o_ids, o_sc = wix.search(Qd, nc=nc, K=K, k_top=k_top, masks=masks)
+        else:
+            o_ids, o_sc = sharded_search(wix, Qd, world, rank, shard["pid_base"], nc=nc, K=K, k_top=k_top,
+                                         masks=masks)
         ids_h[i].copy_(o_ids.to(torch.int32), non_blocking=True)
         sc_h[i].copy_(o_sc, non_blocking=True)
     e3.record(stream)
@@ -378,7 +383,7 @@ def run_ours(args, cfg, rank, world, local):
     cand_tokens //= args.steps
     n_cand //= args.steps
     peaks, peak_kind = load_peaks()
-    s2_flops = 2.0 * B * 32 * wix.NC * 128
+    s2_flops = 2.0 * -(-B // world) * 32 * wix.NC * 128       # this rank's query slice
     s3_bytes = (3.0 * st2["distinct_postings"] + 8.0 * st2["touched"]) / args.steps
     s4_bytes = 36.0 * cand_tokens + 16.0 * n_cand
     stages = {
@@ -427,7 +432,7 @@ def run_ours(args, cfg, rank, world, local):
             "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": f"{args.config}: {cfg['desc']}", "batch": B, "nprobe": nc,
                        "candidates_per_shard": K, "top_k": k_top, "docs": cfg["num_docs"],
-                       "parallelism": f"doc-sharded x{world}" if world > 1 else "single GPU",
+                       "parallelism": f"doc-sharded x{world}, Stage 2 split by query" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (index ~9 GB) and a distinct query batch per step"},
             "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": int(Q[0].numel() * 2),
                     "d2h_bytes_per_step": int(B * k_top * 8)},

@@ -8,6 +8,12 @@ plain-IVF index over local pids, runs Stages 2-4 locally and produces its top-k 
 reference's torch::topk at src/optix_corr_torch_3d.cpp:603-606 leaves ties unspecified).  The
 result equals running each shard alone and merging; because the
 candidate budget applies per shard it is not the 1-GPU result over the union of shards.
+
+Stage 2 (query tokens x centroids) does not depend on the shard, so `sharded_search` does not
+repeat it on every rank: rank r scores its slice of the query batch and `gather_probes` gives
+every rank the whole batch's probe lists with one all-gather.  Stage 2 is exact and each query's
+result is independent of the rest of the batch, so this equals every rank running Stage 2 on
+the whole batch.
 """
 import torch
 
@@ -48,3 +54,53 @@ def merge_topk(ids, scores, world, k_top, pid_base, group=None):
     sc, pid = torch.gather(sc, 1, order), torch.gather(pid, 1, order)
     order = torch.argsort(sc, dim=1, descending=True, stable=True)       # ... then score desc
     return torch.gather(pid, 1, order)[:, :k_top], torch.gather(sc, 1, order)[:, :k_top]
+
+
+def query_slice(B, world, rank):
+    """Rank `rank`'s slice [lo, hi) of a B-query batch for Stage 2, and the padded slice size."""
+    per = -(-B // world)
+    return min(B, rank * per), min(B, (rank + 1) * per), per
+
+
+def gather_probes(topc, scores, world, B, group=None):
+    """This rank's Stage-2 output for its query slice (topc int32 [per, rows, kc], scores f32
+    [per, rows, kc], rows past the batch padded) -> the whole batch's (topc [B, rows, kc],
+    scores [B, rows, kc]) on every rank, with one all_gather_into_tensor."""
+    import torch.distributed as dist
+    pack = torch.stack([topc.to(torch.int32), scores.to(torch.float32).view(torch.int32)], 0)
+    out = torch.empty(world * 2, *topc.shape, dtype=torch.int32, device=topc.device)
+    dist.all_gather_into_tensor(out, pack.contiguous(), group=group)     # rank-major concatenation
+    out = out.view(world, 2, *topc.shape)
+    t = out[:, 0].reshape(-1, *topc.shape[1:])[:B].contiguous()
+    s = out[:, 1].reshape(-1, *topc.shape[1:])[:B].contiguous().view(torch.float32)
+    return t, s
+
+
+def sharded_search(wix, Q, world, rank, pid_base, nc=32, K=4096, k_top=10, masks=None, events=None, group=None):
+    """The `weft` search of a query batch Q [B, 32, 128] fp16 over a corpus split by doc range:
+    Stage 2 on this rank's query slice, probe lists all-gathered, Stages 1-4 and the top-k on
+    this rank's shard `wix` (local pids + pid_base), then the merge over ranks.  Returns
+    (global pids int64 [B, k_top], scores f32 [B, k_top]), the same on every rank.  `events`:
+    optional 5 torch.cuda.Event recorded before Stage 2, after the probe exchange, after
+    Stages 1-3, after Stage 4 and after the local top-k."""
+    def mark(i):
+        if events is not None:
+            events[i].record()
+    B = Q.shape[0]
+    lo, hi, per = query_slice(B, world, rank)
+    if hi - lo == per:
+        Qs = Q[lo:hi]
+    else:                                        # the last slice of a batch that world does not divide
+        Qs = Q.new_zeros(per, *Q.shape[1:])
+        Qs[:hi - lo] = Q[lo:hi]
+    mark(0)
+    topc, sc, _, _ = wix.centroid_topk(Qs, nc)
+    topc, sc = gather_probes(topc, sc, world, B, group=group)
+    mark(1)
+    pids, _, _ = wix.candidates(topc, sc, K, masks=masks)
+    mark(2)
+    f = wix.tile_maxsim(Q, pids)
+    mark(3)
+    ids, s = wix.final_topk(pids, f, k_top, masks=masks)
+    mark(4)
+    return merge_topk(ids, s, world, k_top, pid_base, group=group)

@@ -116,3 +116,44 @@ def test_three_shards_merged_match_oracle_shards(zipf_corpus):
                 return O.tile_maxsim(oix, Q[b].numpy(), np.array([pid - lo], np.int32))[0]
         raise AssertionError(pid)
     _check(ids, sc, oids, osc, score_of)
+
+
+@pytest.mark.parametrize("world", [2, 8, 32])
+def test_stage2_on_query_slices_equals_whole_batch(zipf_corpus, world):
+    """sharded_search scores each rank's query slice and all-gathers the probe lists: the
+    concatenated slices must equal Stage 2 over the whole batch bit for bit (32 queries over
+    2 ranks use the tensor-core kernel, over 32 ranks the CUDA-core one)."""
+    from ragrt_b200.weft import centroid_topk
+    centres, cents, corp, preds, Q, base = zipf_corpus
+    Qb = synth.make_queries(centres, 32, seed=5, topic_zipf=1.1).reshape(32, 32, 128).cuda()
+    C = cents.cuda()
+    t_all, s_all, _, _ = centroid_topk(Qb, C, 16)
+    parts_t, parts_s = [], []
+    for r in range(world):
+        lo, hi, per = shard.query_slice(32, world, r)
+        t, s, _, _ = centroid_topk(Qb[lo:hi], C, 16)
+        parts_t.append(t)
+        parts_s.append(s)
+    assert torch.equal(torch.cat(parts_t), t_all)
+    assert torch.equal(torch.cat(parts_s), s_all)
+
+
+def test_sharded_search_single_rank_equals_search(zipf_corpus):
+    import socket
+    import torch.distributed as dist
+    centres, cents, corp, preds, Q, base = zipf_corpus
+    N = corp["doclens"].shape[0]
+    d, E, pb = _index(corp, preds, cents, base, 0, N, max_len=65535)
+    wix = _weft(d, E)
+    Qc = Q.reshape(-1, 32, 128).cuda()
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        ids, sc = shard.sharded_search(wix, Qc, 1, 0, pb, nc=32, K=400, k_top=10)
+    finally:
+        dist.destroy_process_group()
+    rids, rsc = wix.search(Qc, nc=32, K=400, k_top=10)
+    assert torch.equal(ids, rids.to(torch.int64)) and torch.equal(sc, rsc)

@@ -108,3 +108,69 @@ def test_two_rank_gloo_merge_matches_single_process():
         np.testing.assert_array_equal(got[r][1], exp_sc)
     # the merge really mixes both shards
     assert (exp_ids >= shard.shard_range(small_corpus()[0]["doc_lens"].shape[0], 1, WORLD)[0]).any()
+
+
+def _probes(Q, C, nc):
+    """Stage 2 of each query (the oracle): topc int32 [n, 32, nc], scores f32 [n, 32, nc]."""
+    from oracle import oracle as O
+    ts, ss = [], []
+    for q in Q:
+        t, s, _, _ = O.native_prep(q.numpy(), C, nc, impute=True)
+        ts.append(torch.from_numpy(np.ascontiguousarray(t, dtype=np.int32)))
+        ss.append(torch.from_numpy(np.ascontiguousarray(s, dtype=np.float32)))
+    return torch.stack(ts), torch.stack(ss)
+
+
+def _probe_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        d, Q, _, _ = small_corpus()
+        Q = Q.reshape(-1, 32, 128)[:5]                   # 5 queries over 2 ranks: the last slice is padded
+        C = d["centroids"].numpy()
+        B = Q.shape[0]
+        lo, hi, per = shard.query_slice(B, world, rank)
+        t, s = _probes(Q[lo:hi], C, 8)
+        pad = per - (hi - lo)
+        if pad:
+            t = torch.cat([t, torch.zeros(pad, *t.shape[1:], dtype=t.dtype)])
+            s = torch.cat([s, torch.zeros(pad, *s.shape[1:], dtype=s.dtype)])
+        gt, gs = shard.gather_probes(t, s, world, B)
+        q.put((rank, gt.numpy(), gs.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_probe_exchange_equals_whole_batch():
+    """The Stage-2 split of sharded_search: each rank scores its query slice and gather_probes
+    rebuilds the whole batch's probe lists on every rank, equal to scoring the whole batch."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_probe_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(WORLD):
+        r, t, s = q.get(timeout=180)
+        got[r] = (t, s)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    d, Q, _, _ = small_corpus()
+    et, es = _probes(Q.reshape(-1, 32, 128)[:5], d["centroids"].numpy(), 8)
+    for r in range(WORLD):
+        np.testing.assert_array_equal(got[r][0], et.numpy())
+        np.testing.assert_array_equal(got[r][1], es.numpy())
+
+
+def test_query_slices_cover_batch():
+    for B in (1, 5, 256, 257):
+        for world in (1, 2, 3, 8):
+            seen = []
+            for r in range(world):
+                lo, hi, per = shard.query_slice(B, world, r)
+                assert 0 <= hi - lo <= per and per * world >= B
+                seen.extend(range(lo, hi))
+            assert seen == list(range(B))
