@@ -86,7 +86,7 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 50 ms, started before the warm-up so
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms, started before the warm-up so
     that it is running when the timed region begins; `summary` keeps the samples whose own
     nvidia-smi timestamp lies inside the window set by `mark_start` / `mark_end`."""
     Q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
@@ -110,7 +110,7 @@ class ClockSampler:
             # line-buffered (stdbuf) so that each sample reaches the reader when it is taken
             pre = ["stdbuf", "-oL"] if shutil.which("stdbuf") else []
             self.proc = subprocess.Popen(pre + ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -124,7 +124,7 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc:
-            time.sleep(0.2)                      # the samples of the region's last 50 ms
+            time.sleep(0.2)                      # the samples of the region's last interval
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -152,7 +152,7 @@ class ClockSampler:
         window = (self.t1 - self.t0).total_seconds() if self.t0 and self.t1 else None
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax or None,
                 "reasons": sorted(reasons), "samples": len(sm), "window_s": window,
-                "interval_ms": 50}
+                "interval_ms": 20}
 
 
 def dist_setup(n_gpus):
