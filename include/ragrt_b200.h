@@ -224,7 +224,8 @@ const char* ragrt_last_error(void);
 /*
  * Device-side failure status of the current device since the last reset: 0 none, 1 a kernel
  * gave up a bounded wait (a tensor-core pipeline stage that never completed), 2 a code
- * outside [0, num_centroids) was met (the centroid row was not read), 3 the self-test below;
+ * outside [0, num_centroids) was met (the centroid row was not read), 3 the self-test below,
+ * 4 a token id outside the vocabulary (ragrt_enc_embed);
  * <0 on error.  Synchronises with the device's error flag.  reset != 0 clears it.
  */
 int ragrt_device_error(int32_t reset);
@@ -239,6 +240,49 @@ uint64_t ragrt_launch_count(void);
  * ragrt_device_error).  The CUDA context stays usable.
  */
 int ragrt_selftest_wait_timeout(uint32_t polls, void* stream);
+
+/* ------------------------------------------------------------------------------------ *
+ * Stage 0a: the ColBERT query encoder (BERT-base over [B, 32] query tokens, then ColBERT's
+ * linear 768 -> 128 and L2 normalisation).  Replaces the reference's flat forward
+ * (src/fast_encoder.py:57-77: embeddings + LayerNorm, 12 x [self-attention, LayerNorm, GELU
+ * MLP, LayerNorm], linear, normalize), one kernel per operation; ragrt_b200/encoder.py
+ * strings them together and captures them in a CUDA graph.  All matrices fp16 row-major.
+ * ------------------------------------------------------------------------------------ */
+
+/*
+ * d_out[M, N] = epilogue(d_A[M, K] . d_W[N, K]^T) on the tensor cores, fp32 accumulation.
+ * The nn.Linear products of the reference (F.linear(x, w, b), fast_encoder.py:70-76).
+ *   epilogue 0: + d_bias[N]                 (Q, K, V projection)
+ *   epilogue 1: gelu(+ d_bias), erf form    (intermediate dense, hidden_act "gelu")
+ *   epilogue 2: gelu(+ d_bias), tanh form   (hidden_act "gelu_new")
+ *   epilogue 3: + d_bias + d_residual[M, N] (attention output / output dense + residual)
+ *   epilogue 4: fp16 rounding, then each row divided by its L2 norm (ColBERT linear + F.normalize,
+ *               no bias; N must be 128)
+ * N a multiple of 128, K a multiple of 64, all pointers 16-byte aligned; d_bias may be NULL.
+ */
+int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual, void* d_out,
+                   int32_t M, int32_t N, int32_t K, int32_t epilogue, void* stream);
+
+/* LayerNorm of d_x[rows, dim] (fp32 statistics) with d_gamma / d_beta [dim]; dim 768. */
+int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const void* d_beta, float eps, void* d_out,
+                        int32_t rows, int32_t dim, void* stream);
+
+/*
+ * d_out[B*L, dim] = LayerNorm(word[d_ids] + pos[0..L) + type) (fast_encoder.py:60-63); ids
+ * outside [0, vocab) read row 0 and set the device error flag to 4.  dim 768.
+ */
+int ragrt_enc_embed(const int64_t* d_ids, const void* d_word, const void* d_pos, const void* d_type,
+                    const void* d_gamma, const void* d_beta, float eps, int32_t vocab, int32_t B, int32_t L,
+                    int32_t dim, void* d_out, void* stream);
+
+/*
+ * Multi-head self-attention of each query's L = 32 tokens: d_qkv[B*L, 3*dim] holds Q, K, V in
+ * column blocks of dim, heads of 64 columns; keys with d_mask[b, j] == 0 are not attended
+ * (the reference's additive finfo.min bias); softmax(q k^T / 8) v -> d_ctx[B*L, dim]
+ * (F.scaled_dot_product_attention, fast_encoder.py:71-72).
+ */
+int ragrt_enc_attention(const void* d_qkv, const int64_t* d_mask, void* d_ctx, int32_t B, int32_t L, int32_t heads,
+                        int32_t dim, void* stream);
 
 /* Library version string. */
 const char* ragrt_version(void);

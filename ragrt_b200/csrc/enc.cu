@@ -1,0 +1,493 @@
+// enc.cu -- Stage 0a, the ColBERT query encoder (BERT-base over [B, 32] query tokens, ColBERT's
+// linear 768 -> 128, L2 normalisation), as sm_100a kernels.  Same network and operation order
+// as the reference's flat forward (fast_encoder.py:57-77):
+//   x = LN(word[ids] + pos[0..L) + type[0])
+//   per layer: qkv = x Wqkv^T + b; ctx = softmax(q k^T / sqrt(d) + maskbias) v (per head);
+//              x = LN(x + ctx Wo^T + bo); x = LN(x + gelu(x Wi^T + bi) Wf^T + bf)
+//   out = normalize(fp16(x Wl^T)) per token
+//
+//   enc_gemm       D[M, N] = A[M, K] . W[N, K]^T on the tensor cores (tcgen05.mma kind::f16,
+//                  fp32 accumulators in tensor memory), A and W tiles brought in by TMA
+//                  (128-byte swizzle, K-major, no multicast).  Fused epilogues: + bias,
+//                  gelu (erf or tanh form), + residual, or the final fp16 rounding + L2
+//                  normalisation of a 128-wide row.  Warp 0 issues the TMA loads, warp 1 the
+//                  MMAs, warps 2-5 drain the accumulator (one 32-row quadrant each).
+//   enc_embed_ln   embedding sum + LayerNorm, a warp per token row.
+//   enc_layernorm  LayerNorm of a [rows, dim] fp16 matrix, a warp per row (fp32 statistics).
+//   enc_attention  one warp per (query, head): 32 tokens x head_dim 64; scores, masked
+//                  softmax and the weighted sum in fp32 (the 32 x 32 products are too small
+//                  for the tensor cores to pay).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace ragrt {
+
+namespace {
+
+constexpr int kEM = 128;                 // rows per tile (MMA M)
+constexpr int kEN = 128;                 // columns per tile (MMA N)
+constexpr int kEK = 64;                  // K per stage: one 128-byte swizzle atom of fp16
+constexpr int kEStages = 4;
+constexpr int kETileA = kEM * kEK * 2;   // 16 KB
+constexpr int kETileB = kEN * kEK * 2;   // 16 KB
+constexpr int kEThreads = 192;           // 6 warps
+constexpr uint32_t kEWaitLimit = 1u << 26;
+constexpr int kESmem = 1024 + kEStages * (kETileA + kETileB) + 256;
+
+enum EncEpilogue : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiBiasGeluTanh = 2, kEpiBiasResidual = 3, kEpiNorm = 4 };
+
+struct EncGemmParams {
+    int M, N, K, epi;
+    const __half* bias;       // [N] or null
+    const __half* residual;   // [M, N] or null
+    __half* out;              // [M, N]
+    int* err;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.0f + tanhf(u));
+}
+
+__global__ void __launch_bounds__(kEThreads, 1)
+enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, EncGemmParams p) {
+    extern __shared__ uint8_t enc_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)enc_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = sm;
+    uint8_t* sB = sm + kEStages * kETileA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kEStages * kETileB);
+    uint64_t* empty = full + kEStages;
+    uint64_t* accf = empty + kEStages;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kEN, m0 = blockIdx.y * kEM;
+    const int nk = p.K / kEK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kEStages; ++s) {
+            tc::mbar_init(full + s, 1);
+            tc::mbar_init(empty + s, 1);
+        }
+        tc::mbar_init(accf, 1);
+        *abort = 0;
+        tc::mbar_fence_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tslot, kEN);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tbase = *tslot;
+    bool failed = false;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % kEStages;
+                if (i >= kEStages && !tc::mbar_wait_or_abort(empty + s, ((i / kEStages) - 1) & 1, abort, kEWaitLimit)) {
+                    failed = true;
+                    break;
+                }
+                tc::mbar_arrive_expect_tx(full + s, kETileA + kETileB);
+                tc::tma_load_2d(sA + s * kETileA, &tmA, i * kEK, m0, full + s);
+                tc::tma_load_2d(sB + s * kETileB, &tmW, i * kEK, n0, full + s);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_f16_f32(kEM, kEN);
+            int issued = 0;
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % kEStages;
+                if (!tc::mbar_wait_or_abort(full + s, (i / kEStages) & 1, abort, kEWaitLimit)) {
+                    failed = true;
+                    break;
+                }
+                tc::fence_after();
+                const uint32_t a = tc::smem_u32(sA + s * kETileA), b = tc::smem_u32(sB + s * kETileB);
+#pragma unroll
+                for (int k = 0; k < kEK / 16; ++k)
+                    tc::mma_ss(tbase, tc::sw128_kmajor_desc(a + 32 * k), tc::sw128_kmajor_desc(b + 32 * k), idesc,
+                               (i | k) != 0);
+                tc::mma_commit(empty + s);
+                issued = i + 1;
+            }
+            if (!failed) tc::mma_commit(accf);
+            else if (issued > 0)     // the last MMAs read shared memory: let them finish
+                (void)tc::mbar_wait_bounded(empty + (issued - 1) % kEStages, ((issued - 1) / kEStages) & 1, kEWaitLimit);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quad = warp & 3;
+        const int row = m0 + quad * 32 + lane;
+        const bool ok = tc::mbar_wait_or_abort(accf, 0, abort, kEWaitLimit);
+        if (__all_sync(0xFFFFFFFFu, ok)) {
+            tc::fence_after();
+            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16);
+            if (p.epi == kEpiNorm) {
+                // the whole 128-wide row is in this thread: fp16 rounding, then L2 norm in fp32
+                float v[kEN];
+#pragma unroll
+                for (int c = 0; c < kEN / 32; ++c) {
+                    uint32_t r[32];
+                    tc::ld32x32(taddr + 32 * c, r);
+                    tc::wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[32 * c + j] = __half2float(__float2half_rn(__uint_as_float(r[j])));
+                }
+                float ss = 0.f;
+#pragma unroll
+                for (int j = 0; j < kEN; ++j) ss = fmaf(v[j], v[j], ss);
+                const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+                if (row < p.M) {
+                    __half* o = p.out + (int64_t)row * p.N + n0;
+#pragma unroll
+                    for (int j = 0; j < kEN; j += 8) {
+                        uint4 u;
+                        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) h[t] = __floats2half2_rn(v[j + 2 * t] * inv, v[j + 2 * t + 1] * inv);
+                        *reinterpret_cast<uint4*>(o + j) = u;
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kEN / 32; ++c) {
+                    uint32_t r[32];
+                    tc::ld32x32(taddr + 32 * c, r);
+                    tc::wait_ld();
+                    if (row < p.M) {
+                        const int col = n0 + 32 * c;
+                        const __half* bp = p.bias ? p.bias + col : nullptr;
+                        const __half* rp = p.epi == kEpiBiasResidual ? p.residual + (int64_t)row * p.N + col : nullptr;
+                        __half* o = p.out + (int64_t)row * p.N + col;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            float f[8];
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) f[t] = __uint_as_float(r[j + t]);
+                            if (bp) {
+                                const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bp + j));
+                                const __half2* bh = reinterpret_cast<const __half2*>(&bu);
+#pragma unroll
+                                for (int t = 0; t < 4; ++t) {
+                                    const float2 b2 = __half22float2(bh[t]);
+                                    f[2 * t] += b2.x;
+                                    f[2 * t + 1] += b2.y;
+                                }
+                            }
+                            if (p.epi == kEpiBiasGelu) {
+#pragma unroll
+                                for (int t = 0; t < 8; ++t) f[t] = gelu_erf(f[t]);
+                            } else if (p.epi == kEpiBiasGeluTanh) {
+#pragma unroll
+                                for (int t = 0; t < 8; ++t) f[t] = gelu_tanh(f[t]);
+                            } else if (rp) {
+                                const uint4 ru = *reinterpret_cast<const uint4*>(rp + j);
+                                const __half2* rh = reinterpret_cast<const __half2*>(&ru);
+#pragma unroll
+                                for (int t = 0; t < 4; ++t) {
+                                    const float2 r2 = __half22float2(rh[t]);
+                                    f[2 * t] += r2.x;
+                                    f[2 * t + 1] += r2.y;
+                                }
+                            }
+                            uint4 u;
+                            __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) h[t] = __floats2half2_rn(f[2 * t], f[2 * t + 1]);
+                            *reinterpret_cast<uint4*>(o + j) = u;
+                        }
+                    }
+                }
+            }
+        } else {
+            failed = true;
+        }
+    }
+    if (failed && lane == 0) atomicExch(p.err, 1);
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after();
+        tc::tmem_dealloc(tbase, kEN);
+    }
+}
+
+// LayerNorm of one row held by a warp: 8 fp16 per lane per 256 columns.
+template <int kDimT>
+__device__ __forceinline__ void warp_layernorm_store(float (&v)[kDimT / 32], const __half* gamma, const __half* beta,
+                                                     float eps, __half* out, int lane) {
+    constexpr int kPer = kDimT / 32;
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) s += v[i];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    const float mean = s * (1.0f / kDimT);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const float d = v[i] - mean;
+        q = fmaf(d, d, q);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
+    const float rstd = rsqrtf(q * (1.0f / kDimT) + eps);
+#pragma unroll
+    for (int g = 0; g < kPer / 8; ++g) {
+        const int col = (g * 32 + lane) * 8;
+        const uint4 gu = __ldg(reinterpret_cast<const uint4*>(gamma + col));
+        const uint4 bu = __ldg(reinterpret_cast<const uint4*>(beta + col));
+        const __half2* gh = reinterpret_cast<const __half2*>(&gu);
+        const __half2* bh = reinterpret_cast<const __half2*>(&bu);
+        uint4 u;
+        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float2 g2 = __half22float2(gh[t]), b2 = __half22float2(bh[t]);
+            h[t] = __floats2half2_rn((v[g * 8 + 2 * t] - mean) * rstd * g2.x + b2.x,
+                                     (v[g * 8 + 2 * t + 1] - mean) * rstd * g2.y + b2.y);
+        }
+        *reinterpret_cast<uint4*>(out + col) = u;
+    }
+}
+
+template <int kDimT>
+__device__ __forceinline__ void load_row(const __half* src, float (&v)[kDimT / 32], int lane) {
+#pragma unroll
+    for (int g = 0; g < kDimT / 256; ++g) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + (g * 32 + lane) * 8);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float2 f = __half22float2(h[t]);
+            v[g * 8 + 2 * t] = f.x;
+            v[g * 8 + 2 * t + 1] = f.y;
+        }
+    }
+}
+
+template <int kDimT>
+__global__ void enc_layernorm(const __half* __restrict__ x, const __half* __restrict__ gamma,
+                              const __half* __restrict__ beta, float eps, __half* __restrict__ out, int rows) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    float v[kDimT / 32];
+    load_row<kDimT>(x + (int64_t)warp * kDimT, v, lane);
+    warp_layernorm_store<kDimT>(v, gamma, beta, eps, out + (int64_t)warp * kDimT, lane);
+}
+
+// x[row] = LN(word[ids[row]] + pos[row % L] + type), summed in fp32 (token ids outside the
+// vocabulary are clamped to 0 and raise the error word)
+template <int kDimT>
+__global__ void enc_embed_ln(const int64_t* __restrict__ ids, const __half* __restrict__ word,
+                             const __half* __restrict__ pos, const __half* __restrict__ type,
+                             const __half* __restrict__ gamma, const __half* __restrict__ beta, float eps, int vocab,
+                             int L, int rows, __half* __restrict__ out, int* err) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    int64_t id = ids[warp];
+    if (id < 0 || id >= vocab) {
+        if (lane == 0) atomicExch(err, 4);
+        id = 0;
+    }
+    float v[kDimT / 32], a[kDimT / 32], b[kDimT / 32];
+    load_row<kDimT>(word + id * kDimT, v, lane);
+    load_row<kDimT>(pos + (int64_t)(warp % L) * kDimT, a, lane);
+    load_row<kDimT>(type, b, lane);
+#pragma unroll
+    for (int i = 0; i < kDimT / 32; ++i) v[i] += a[i] + b[i];
+    warp_layernorm_store<kDimT>(v, gamma, beta, eps, out + (int64_t)warp * kDimT, lane);
+}
+
+// One warp per (query, head); lane i = query token i (L = 32), head_dim 64.  qkv [B*L, 3*D]
+// with Q, K, V in column blocks of D; mask [B, L] (1 = attended key); ctx [B*L, D].
+constexpr int kHd = 64;
+constexpr int kAttWarps = 2;
+__global__ void __launch_bounds__(kAttWarps * 32)
+enc_attention(const __half* __restrict__ qkv, const int64_t* __restrict__ mask, __half* __restrict__ ctx, int B,
+              int H, int D, float scale) {
+    __shared__ float sK[kAttWarps][32][kHd + 1];
+    __shared__ float sV[kAttWarps][32][kHd + 1];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int item = blockIdx.x * kAttWarps + w;
+    if (item >= B * H) return;
+    const int b = item / H, h = item % H;
+    const int64_t row = (int64_t)b * 32 + lane;
+    const __half* base = qkv + row * (3 * D) + h * kHd;
+    float q[kHd];
+#pragma unroll
+    for (int g = 0; g < kHd / 8; ++g) {
+        const uint4 uq = *reinterpret_cast<const uint4*>(base + g * 8);
+        const uint4 uk = *reinterpret_cast<const uint4*>(base + D + g * 8);
+        const uint4 uv = *reinterpret_cast<const uint4*>(base + 2 * D + g * 8);
+        const __half2* hq = reinterpret_cast<const __half2*>(&uq);
+        const __half2* hk = reinterpret_cast<const __half2*>(&uk);
+        const __half2* hv = reinterpret_cast<const __half2*>(&uv);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float2 fq = __half22float2(hq[t]), fk = __half22float2(hk[t]), fv = __half22float2(hv[t]);
+            q[g * 8 + 2 * t] = fq.x;
+            q[g * 8 + 2 * t + 1] = fq.y;
+            sK[w][lane][g * 8 + 2 * t] = fk.x;
+            sK[w][lane][g * 8 + 2 * t + 1] = fk.y;
+            sV[w][lane][g * 8 + 2 * t] = fv.x;
+            sV[w][lane][g * 8 + 2 * t + 1] = fv.y;
+        }
+    }
+    const bool keep = mask[row] != 0;
+    const unsigned kept = __ballot_sync(0xFFFFFFFFu, keep);
+    __syncwarp();
+    float s[32];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        float d = 0.f;
+#pragma unroll
+        for (int k = 0; k < kHd; ++k) d = fmaf(q[k], sK[w][j][k], d);
+        s[j] = ((kept >> j) & 1u) ? d * scale : -INFINITY;
+        mx = fmaxf(mx, s[j]);
+    }
+    float o[kHd];
+#pragma unroll
+    for (int k = 0; k < kHd; ++k) o[k] = 0.f;
+    float den = 0.f;
+    if (mx != -INFINITY) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float e = __expf(s[j] - mx);
+            den += e;
+#pragma unroll
+            for (int k = 0; k < kHd; ++k) o[k] = fmaf(e, sV[w][j][k], o[k]);
+        }
+    }
+    const float inv = den > 0.f ? 1.0f / den : 0.f;
+    __half* out = ctx + row * D + h * kHd;
+#pragma unroll
+    for (int g = 0; g < kHd / 8; ++g) {
+        uint4 u;
+        __half2* hh = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) hh[t] = __floats2half2_rn(o[g * 8 + 2 * t] * inv, o[g * 8 + 2 * t + 1] * inv);
+        *reinterpret_cast<uint4*>(out + g * 8) = u;
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn enc_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)f;
+    }
+    return fn;
+}
+
+// fp16 [rows, cols] row-major, box [box_rows x 64 cols], 128-byte swizzle (out-of-range rows read 0)
+int enc_make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+    EncodeTiledFn fn = enc_encode_fn();
+    if (!fn) return fail(RAGRT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kEK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(RAGRT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return RAGRT_OK;
+}
+
+}  // namespace
+}  // namespace ragrt
+
+using namespace ragrt;
+
+extern "C" int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual, void* d_out,
+                              int32_t M, int32_t N, int32_t K, int32_t epilogue, void* stream_) {
+    cudaStream_t stream = (cudaStream_t)stream_;
+    RAGRT_REQUIRE(d_A && d_W && d_out, "null argument");
+    RAGRT_REQUIRE(M >= 1 && N >= kEN && N % kEN == 0 && K >= kEK && K % kEK == 0,
+                  "enc_gemm needs M >= 1, N a multiple of %d and K a multiple of %d (M=%d N=%d K=%d)", kEN, kEK,
+                  (int)M, (int)N, (int)K);
+    RAGRT_REQUIRE(epilogue >= kEpiBias && epilogue <= kEpiNorm, "unknown epilogue %d", (int)epilogue);
+    RAGRT_REQUIRE(epilogue != kEpiNorm || N == kEN, "the normalising epilogue needs N == %d", kEN);
+    RAGRT_REQUIRE(epilogue != kEpiBiasResidual || d_residual, "the residual epilogue needs a residual");
+    RAGRT_REQUIRE(((uintptr_t)d_A & 15) == 0 && ((uintptr_t)d_W & 15) == 0 && ((uintptr_t)d_out & 15) == 0 &&
+                      ((uintptr_t)d_bias & 15) == 0 && ((uintptr_t)d_residual & 15) == 0,
+                  "enc_gemm operands must be 16-byte aligned");
+    int* err = device_error_flag();
+    if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
+    CUtensorMap tA, tW;
+    int rc = enc_make_map(&tA, d_A, M, K, kEM);
+    if (rc || (rc = enc_make_map(&tW, d_W, N, K, kEN))) return rc;
+    static bool attr = false;
+    if (!attr) {
+        RAGRT_CUDA_TRY(cudaFuncSetAttribute(enc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kESmem));
+        attr = true;
+    }
+    EncGemmParams p{M, N, K, epilogue, (const __half*)d_bias, (const __half*)d_residual, (__half*)d_out, err};
+    dim3 grid((unsigned)(N / kEN), (unsigned)ceil_div(M, kEM));
+    enc_gemm<<<grid, kEThreads, kESmem, stream>>>(tA, tW, p);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}
+
+extern "C" int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const void* d_beta, float eps, void* d_out,
+                                   int32_t rows, int32_t dim, void* stream_) {
+    RAGRT_REQUIRE(d_x && d_gamma && d_beta && d_out, "null argument");
+    RAGRT_REQUIRE(dim == 768, "enc_layernorm is built for dim 768 (BERT-base); got %d", (int)dim);
+    RAGRT_REQUIRE(rows >= 0, "rows must be >= 0");
+    if (rows == 0) return RAGRT_OK;
+    const int threads = 256;
+    enc_layernorm<768><<<(unsigned)ceil_div((int64_t)rows * 32, threads), threads, 0, (cudaStream_t)stream_>>>(
+        (const __half*)d_x, (const __half*)d_gamma, (const __half*)d_beta, eps, (__half*)d_out, rows);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}
+
+extern "C" int ragrt_enc_embed(const int64_t* d_ids, const void* d_word, const void* d_pos, const void* d_type,
+                               const void* d_gamma, const void* d_beta, float eps, int32_t vocab, int32_t B, int32_t L,
+                               int32_t dim, void* d_out, void* stream_) {
+    RAGRT_REQUIRE(d_ids && d_word && d_pos && d_type && d_gamma && d_beta && d_out, "null argument");
+    RAGRT_REQUIRE(dim == 768, "enc_embed is built for dim 768 (BERT-base); got %d", (int)dim);
+    RAGRT_REQUIRE(B >= 1 && L >= 1 && vocab >= 1, "B, L and vocab must be >= 1");
+    int* err = device_error_flag();
+    if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
+    const int rows = B * L, threads = 256;
+    enc_embed_ln<768><<<(unsigned)ceil_div((int64_t)rows * 32, threads), threads, 0, (cudaStream_t)stream_>>>(
+        d_ids, (const __half*)d_word, (const __half*)d_pos, (const __half*)d_type, (const __half*)d_gamma,
+        (const __half*)d_beta, eps, vocab, L, rows, (__half*)d_out, err);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}
+
+extern "C" int ragrt_enc_attention(const void* d_qkv, const int64_t* d_mask, void* d_ctx, int32_t B, int32_t L,
+                                   int32_t heads, int32_t dim, void* stream_) {
+    RAGRT_REQUIRE(d_qkv && d_mask && d_ctx, "null argument");
+    RAGRT_REQUIRE(L == 32, "enc_attention is built for 32 query tokens; got %d", (int)L);
+    RAGRT_REQUIRE(heads >= 1 && dim == heads * kHd, "enc_attention needs head_dim %d (dim %d, heads %d)", kHd,
+                  (int)dim, (int)heads);
+    RAGRT_REQUIRE(B >= 1, "B must be >= 1");
+    const int items = B * heads;
+    enc_attention<<<(unsigned)ceil_div(items, kAttWarps), kAttWarps * 32, 0, (cudaStream_t)stream_>>>(
+        (const __half*)d_qkv, d_mask, (__half*)d_ctx, B, heads, dim, 1.0f / sqrtf((float)kHd));
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}
