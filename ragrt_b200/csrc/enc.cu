@@ -14,10 +14,12 @@
 //                  MMAs, warps 2-5 drain the accumulator (one 32-row quadrant each).
 //   enc_embed_ln   embedding sum + LayerNorm, a warp per token row.
 //   enc_layernorm  LayerNorm of a [rows, dim] fp16 matrix, a warp per row (fp32 statistics).
-//   enc_attention  one warp per (query, head): 32 tokens x head_dim 64; scores, masked
+//   enc_attention  two warps per (query, head): 32 tokens x head_dim 64; scores, masked
 //                  softmax and the weighted sum in fp32 (the 32 x 32 products are too small
 //                  for the tensor cores to pay).
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -27,14 +29,19 @@ namespace ragrt {
 namespace {
 
 constexpr int kEM = 128;                 // rows per tile (MMA M)
-constexpr int kEN = 128;                 // columns per tile (MMA N)
 constexpr int kEK = 64;                  // K per stage: one 128-byte swizzle atom of fp16
-constexpr int kEStages = 4;
 constexpr int kETileA = kEM * kEK * 2;   // 16 KB
-constexpr int kETileB = kEN * kEK * 2;   // 16 KB
 constexpr int kEThreads = 192;           // 6 warps
 constexpr uint32_t kEWaitLimit = 1u << 26;
-constexpr int kESmem = 1024 + kEStages * (kETileA + kETileB) + 256;
+constexpr int kEStageBudget = 192 * 1024;
+
+template <int BN>
+struct EncCfg {
+    static constexpr int kTileB = BN * kEK * 2;
+    static constexpr int kStages = kEStageBudget / (kETileA + kTileB);
+    static constexpr int kSmem = 1024 + kStages * (kETileA + kTileB) + 256;
+    static constexpr uint32_t kTmemCols = 2 * BN;       // two accumulator buffers
+};
 
 enum EncEpilogue : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiBiasGeluTanh = 2, kEpiBiasResidual = 3, kEpiNorm = 4 };
 
@@ -52,33 +59,45 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.0f + tanhf(u));
 }
 
+// Persistent: CTA c takes tiles c, c + grid, ... (N-tile index fastest, so neighbouring CTAs
+// share the A row block).  The TMA ring runs across tile boundaries; the MMA warp alternates
+// between two accumulator buffers in tensor memory so that the epilogue of one tile overlaps
+// the main loop of the next.
+template <int BN>
 __global__ void __launch_bounds__(kEThreads, 1)
 enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, EncGemmParams p) {
+    using Cfg = EncCfg<BN>;
+    constexpr int S = Cfg::kStages;
     extern __shared__ uint8_t enc_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)enc_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = sm;
-    uint8_t* sB = sm + kEStages * kETileA;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kEStages * kETileB);
-    uint64_t* empty = full + kEStages;
-    uint64_t* accf = empty + kEStages;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+    uint8_t* sB = sm + S * kETileA;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kTileB);
+    uint64_t* empty = full + S;
+    uint64_t* accf = empty + S;          // [2] accumulator ready (MMA -> epilogue)
+    uint64_t* acce = accf + 2;           // [2] accumulator drained (epilogue -> MMA)
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(acce + 2);
     volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kEN, m0 = blockIdx.y * kEM;
     const int nk = p.K / kEK;
+    const int tiles_n = p.N / BN;
+    const int tiles = tiles_n * (int)((p.M + kEM - 1) / kEM);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kEStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             tc::mbar_init(full + s, 1);
             tc::mbar_init(empty + s, 1);
         }
-        tc::mbar_init(accf, 1);
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(accf + b, 1);
+            tc::mbar_init(acce + b, 4);
+        }
         *abort = 0;
         tc::mbar_fence_init();
     }
     if (warp == 1) {
-        tc::tmem_alloc(tslot, kEN);
+        tc::tmem_alloc(tslot, Cfg::kTmemCols);
         tc::tmem_relinquish();
     }
     tc::fence_before();
@@ -90,78 +109,98 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % kEStages;
-                if (i >= kEStages && !tc::mbar_wait_or_abort(empty + s, ((i / kEStages) - 1) & 1, abort, kEWaitLimit)) {
-                    failed = true;
-                    break;
+            int g = 0;                                   // k-chunk counter over all of this CTA's tiles
+            for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * kEM, n0 = (t % tiles_n) * BN;
+                for (int i = 0; i < nk; ++i, ++g) {
+                    const int s = g % S;
+                    if (g >= S && !tc::mbar_wait_or_abort(empty + s, ((g / S) - 1) & 1, abort, kEWaitLimit)) {
+                        failed = true;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(full + s, kETileA + Cfg::kTileB);
+                    tc::tma_load_2d(sA + s * kETileA, &tmA, i * kEK, m0, full + s);
+                    tc::tma_load_2d(sB + s * Cfg::kTileB, &tmW, i * kEK, n0, full + s);
                 }
-                tc::mbar_arrive_expect_tx(full + s, kETileA + kETileB);
-                tc::tma_load_2d(sA + s * kETileA, &tmA, i * kEK, m0, full + s);
-                tc::tma_load_2d(sB + s * kETileB, &tmW, i * kEK, n0, full + s);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_f16_f32(kEM, kEN);
-            int issued = 0;
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % kEStages;
-                if (!tc::mbar_wait_or_abort(full + s, (i / kEStages) & 1, abort, kEWaitLimit)) {
+            constexpr uint32_t idesc = tc::idesc_f16_f32(kEM, BN);
+            int g = 0, j = 0, issued_g = -1;
+            for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++j) {
+                const int b = j & 1;
+                if (j >= 2 && !tc::mbar_wait_or_abort(acce + b, ((j >> 1) - 1) & 1, abort, kEWaitLimit)) {
                     failed = true;
                     break;
                 }
                 tc::fence_after();
-                const uint32_t a = tc::smem_u32(sA + s * kETileA), b = tc::smem_u32(sB + s * kETileB);
+                const uint32_t d = tbase + (uint32_t)(b * BN);
+                for (int i = 0; i < nk; ++i, ++g) {
+                    const int s = g % S;
+                    if (!tc::mbar_wait_or_abort(full + s, (g / S) & 1, abort, kEWaitLimit)) {
+                        failed = true;
+                        break;
+                    }
+                    tc::fence_after();
+                    const uint32_t a = tc::smem_u32(sA + s * kETileA), bb = tc::smem_u32(sB + s * Cfg::kTileB);
 #pragma unroll
-                for (int k = 0; k < kEK / 16; ++k)
-                    tc::mma_ss(tbase, tc::sw128_kmajor_desc(a + 32 * k), tc::sw128_kmajor_desc(b + 32 * k), idesc,
-                               (i | k) != 0);
-                tc::mma_commit(empty + s);
-                issued = i + 1;
+                    for (int k = 0; k < kEK / 16; ++k)
+                        tc::mma_ss(d, tc::sw128_kmajor_desc(a + 32 * k), tc::sw128_kmajor_desc(bb + 32 * k), idesc,
+                                   (i | k) != 0);
+                    tc::mma_commit(empty + s);
+                    issued_g = g;
+                }
+                if (!failed) tc::mma_commit(accf + b);
             }
-            if (!failed) tc::mma_commit(accf);
-            else if (issued > 0)     // the last MMAs read shared memory: let them finish
-                (void)tc::mbar_wait_bounded(empty + (issued - 1) % kEStages, ((issued - 1) / kEStages) & 1, kEWaitLimit);
+            if (failed && issued_g >= 0)   // the last MMAs read shared memory: let them finish
+                (void)tc::mbar_wait_bounded(empty + issued_g % S, (issued_g / S) & 1, kEWaitLimit);
         }
     } else {
         // ------------------------------------------------------------ epilogue
         const int quad = warp & 3;
-        const int row = m0 + quad * 32 + lane;
-        const bool ok = tc::mbar_wait_or_abort(accf, 0, abort, kEWaitLimit);
-        if (__all_sync(0xFFFFFFFFu, ok)) {
+        int j = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+            const int b = j & 1;
+            const int m0 = (t / tiles_n) * kEM, n0 = (t % tiles_n) * BN;
+            const int row = m0 + quad * 32 + lane;
+            const bool ok = tc::mbar_wait_or_abort(accf + b, (j >> 1) & 1, abort, kEWaitLimit);
+            if (!__all_sync(0xFFFFFFFFu, ok)) {
+                failed = true;
+                break;
+            }
             tc::fence_after();
-            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16);
+            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN);
             if (p.epi == kEpiNorm) {
                 // the whole 128-wide row is in this thread: fp16 rounding, then L2 norm in fp32
-                float v[kEN];
+                float v[128];
 #pragma unroll
-                for (int c = 0; c < kEN / 32; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     uint32_t r[32];
                     tc::ld32x32(taddr + 32 * c, r);
                     tc::wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[32 * c + j] = __half2float(__float2half_rn(__uint_as_float(r[j])));
+                    for (int q = 0; q < 32; ++q) v[32 * c + q] = __half2float(__float2half_rn(__uint_as_float(r[q])));
                 }
                 float ss = 0.f;
 #pragma unroll
-                for (int j = 0; j < kEN; ++j) ss = fmaf(v[j], v[j], ss);
+                for (int q = 0; q < 128; ++q) ss = fmaf(v[q], v[q], ss);
                 const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
                 if (row < p.M) {
                     __half* o = p.out + (int64_t)row * p.N + n0;
 #pragma unroll
-                    for (int j = 0; j < kEN; j += 8) {
+                    for (int q = 0; q < 128; q += 8) {
                         uint4 u;
                         __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) h[t] = __floats2half2_rn(v[j + 2 * t] * inv, v[j + 2 * t + 1] * inv);
-                        *reinterpret_cast<uint4*>(o + j) = u;
+                        for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[q + 2 * e] * inv, v[q + 2 * e + 1] * inv);
+                        *reinterpret_cast<uint4*>(o + q) = u;
                     }
                 }
             } else {
 #pragma unroll 1
-                for (int c = 0; c < kEN / 32; ++c) {
+                for (int c = 0; c < BN / 32; ++c) {
                     uint32_t r[32];
                     tc::ld32x32(taddr + 32 * c, r);
                     tc::wait_ld();
@@ -171,47 +210,48 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
                         const __half* rp = p.epi == kEpiBiasResidual ? p.residual + (int64_t)row * p.N + col : nullptr;
                         __half* o = p.out + (int64_t)row * p.N + col;
 #pragma unroll
-                        for (int j = 0; j < 32; j += 8) {
+                        for (int q = 0; q < 32; q += 8) {
                             float f[8];
 #pragma unroll
-                            for (int t = 0; t < 8; ++t) f[t] = __uint_as_float(r[j + t]);
+                            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[q + e]);
                             if (bp) {
-                                const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bp + j));
+                                const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bp + q));
                                 const __half2* bh = reinterpret_cast<const __half2*>(&bu);
 #pragma unroll
-                                for (int t = 0; t < 4; ++t) {
-                                    const float2 b2 = __half22float2(bh[t]);
-                                    f[2 * t] += b2.x;
-                                    f[2 * t + 1] += b2.y;
+                                for (int e = 0; e < 4; ++e) {
+                                    const float2 b2 = __half22float2(bh[e]);
+                                    f[2 * e] += b2.x;
+                                    f[2 * e + 1] += b2.y;
                                 }
                             }
                             if (p.epi == kEpiBiasGelu) {
 #pragma unroll
-                                for (int t = 0; t < 8; ++t) f[t] = gelu_erf(f[t]);
+                                for (int e = 0; e < 8; ++e) f[e] = gelu_erf(f[e]);
                             } else if (p.epi == kEpiBiasGeluTanh) {
 #pragma unroll
-                                for (int t = 0; t < 8; ++t) f[t] = gelu_tanh(f[t]);
+                                for (int e = 0; e < 8; ++e) f[e] = gelu_tanh(f[e]);
                             } else if (rp) {
-                                const uint4 ru = *reinterpret_cast<const uint4*>(rp + j);
+                                const uint4 ru = *reinterpret_cast<const uint4*>(rp + q);
                                 const __half2* rh = reinterpret_cast<const __half2*>(&ru);
 #pragma unroll
-                                for (int t = 0; t < 4; ++t) {
-                                    const float2 r2 = __half22float2(rh[t]);
-                                    f[2 * t] += r2.x;
-                                    f[2 * t + 1] += r2.y;
+                                for (int e = 0; e < 4; ++e) {
+                                    const float2 r2 = __half22float2(rh[e]);
+                                    f[2 * e] += r2.x;
+                                    f[2 * e + 1] += r2.y;
                                 }
                             }
                             uint4 u;
                             __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
-                            for (int t = 0; t < 4; ++t) h[t] = __floats2half2_rn(f[2 * t], f[2 * t + 1]);
-                            *reinterpret_cast<uint4*>(o + j) = u;
+                            for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
+                            *reinterpret_cast<uint4*>(o + q) = u;
                         }
                     }
                 }
             }
-        } else {
-            failed = true;
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(acce + b);
         }
     }
     if (failed && lane == 0) atomicExch(p.err, 1);
@@ -219,7 +259,7 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
     __syncthreads();
     if (warp == 1) {
         tc::fence_after();
-        tc::tmem_dealloc(tbase, kEN);
+        tc::tmem_dealloc(tbase, Cfg::kTmemCols);
     }
 }
 
@@ -310,71 +350,111 @@ __global__ void enc_embed_ln(const int64_t* __restrict__ ids, const __half* __re
     warp_layernorm_store<kDimT>(v, gamma, beta, eps, out + (int64_t)warp * kDimT, lane);
 }
 
-// One warp per (query, head); lane i = query token i (L = 32), head_dim 64.  qkv [B*L, 3*D]
-// with Q, K, V in column blocks of D; mask [B, L] (1 = attended key); ctx [B*L, D].
+// Attention of one (query, head): L = 32 tokens, head_dim 64, two warps.  Lanes 2i and 2i+1
+// own query token i (of the CTA's 16 in warp w: i = 16 w + lane / 2) and half of the head's
+// dimensions each: partial q.k dots are combined with one shuffle, the softmax runs in fp32 on
+// both lanes, and each lane accumulates its half of p.V.  K and V are staged in shared memory
+// as fp32 rows of 68 floats, the second half of a row 4 floats further on (so that the two
+// halves read in one instruction fall in different banks), read as broadcast float4.  qkv [B*L, 3*D] with Q, K, V in column blocks of D; mask [B, L] (1 = attended key);
+// ctx [B*L, D].
 constexpr int kHd = 64;
-constexpr int kAttWarps = 2;
-__global__ void __launch_bounds__(kAttWarps * 32)
+constexpr int kKvStride = 68;
+__global__ void __launch_bounds__(64)
 enc_attention(const __half* __restrict__ qkv, const int64_t* __restrict__ mask, __half* __restrict__ ctx, int B,
               int H, int D, float scale) {
-    __shared__ float sK[kAttWarps][32][kHd + 1];
-    __shared__ float sV[kAttWarps][32][kHd + 1];
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int item = blockIdx.x * kAttWarps + w;
-    if (item >= B * H) return;
-    const int b = item / H, h = item % H;
-    const int64_t row = (int64_t)b * 32 + lane;
-    const __half* base = qkv + row * (3 * D) + h * kHd;
-    float q[kHd];
+    __shared__ __align__(16) float sK[32][kKvStride];
+    __shared__ __align__(16) float sV[32][kKvStride];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int b = blockIdx.x / H, h = blockIdx.x % H;
+    // stage K and V: thread t loads token t / 2, half t % 2 (32 dims = 4 x 16 B) of each
+    {
+        const int tok = tid >> 1, half = tid & 1;
+        const __half* src = qkv + ((int64_t)b * 32 + tok) * (3 * D) + h * kHd + half * 32;
 #pragma unroll
-    for (int g = 0; g < kHd / 8; ++g) {
-        const uint4 uq = *reinterpret_cast<const uint4*>(base + g * 8);
-        const uint4 uk = *reinterpret_cast<const uint4*>(base + D + g * 8);
-        const uint4 uv = *reinterpret_cast<const uint4*>(base + 2 * D + g * 8);
-        const __half2* hq = reinterpret_cast<const __half2*>(&uq);
-        const __half2* hk = reinterpret_cast<const __half2*>(&uk);
-        const __half2* hv = reinterpret_cast<const __half2*>(&uv);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const float2 fq = __half22float2(hq[t]), fk = __half22float2(hk[t]), fv = __half22float2(hv[t]);
-            q[g * 8 + 2 * t] = fq.x;
-            q[g * 8 + 2 * t + 1] = fq.y;
-            sK[w][lane][g * 8 + 2 * t] = fk.x;
-            sK[w][lane][g * 8 + 2 * t + 1] = fk.y;
-            sV[w][lane][g * 8 + 2 * t] = fv.x;
-            sV[w][lane][g * 8 + 2 * t + 1] = fv.y;
+        for (int g = 0; g < 4; ++g) {
+            const uint4 uk = *reinterpret_cast<const uint4*>(src + D + g * 8);
+            const uint4 uv = *reinterpret_cast<const uint4*>(src + 2 * D + g * 8);
+            const __half2* hk = reinterpret_cast<const __half2*>(&uk);
+            const __half2* hv = reinterpret_cast<const __half2*>(&uv);
+            float4 k0, k1, v0, v1;
+            float2 t;
+            t = __half22float2(hk[0]); k0.x = t.x; k0.y = t.y;
+            t = __half22float2(hk[1]); k0.z = t.x; k0.w = t.y;
+            t = __half22float2(hk[2]); k1.x = t.x; k1.y = t.y;
+            t = __half22float2(hk[3]); k1.z = t.x; k1.w = t.y;
+            t = __half22float2(hv[0]); v0.x = t.x; v0.y = t.y;
+            t = __half22float2(hv[1]); v0.z = t.x; v0.w = t.y;
+            t = __half22float2(hv[2]); v1.x = t.x; v1.y = t.y;
+            t = __half22float2(hv[3]); v1.z = t.x; v1.w = t.y;
+            float* kd = &sK[tok][half * 36 + g * 8];
+            float* vd = &sV[tok][half * 36 + g * 8];
+            *reinterpret_cast<float4*>(kd) = k0;
+            *reinterpret_cast<float4*>(kd + 4) = k1;
+            *reinterpret_cast<float4*>(vd) = v0;
+            *reinterpret_cast<float4*>(vd + 4) = v1;
         }
     }
-    const bool keep = mask[row] != 0;
-    const unsigned kept = __ballot_sync(0xFFFFFFFFu, keep);
-    __syncwarp();
+    const int i = w * 16 + (lane >> 1), half = lane & 1;
+    const int64_t row = (int64_t)b * 32 + i;
+    float q[32];
+    {
+        const __half* qs = qkv + row * (3 * D) + h * kHd + half * 32;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const uint4 u = *reinterpret_cast<const uint4*>(qs + g * 8);
+            const __half2* hq = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float2 f = __half22float2(hq[t]);
+                q[g * 8 + 2 * t] = f.x * scale;
+                q[g * 8 + 2 * t + 1] = f.y * scale;
+            }
+        }
+    }
+    const unsigned kept = __ballot_sync(0xFFFFFFFFu, mask[(int64_t)b * 32 + lane] != 0);
+    __syncthreads();
     float s[32];
     float mx = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
+        const float4* kr = reinterpret_cast<const float4*>(&sK[j][half * 36]);
         float d = 0.f;
 #pragma unroll
-        for (int k = 0; k < kHd; ++k) d = fmaf(q[k], sK[w][j][k], d);
-        s[j] = ((kept >> j) & 1u) ? d * scale : -INFINITY;
+        for (int c = 0; c < 8; ++c) {
+            const float4 k4 = kr[c];
+            d = fmaf(q[4 * c], k4.x, d);
+            d = fmaf(q[4 * c + 1], k4.y, d);
+            d = fmaf(q[4 * c + 2], k4.z, d);
+            d = fmaf(q[4 * c + 3], k4.w, d);
+        }
+        d += __shfl_xor_sync(0xFFFFFFFFu, d, 1);
+        s[j] = ((kept >> j) & 1u) ? d : -INFINITY;
         mx = fmaxf(mx, s[j]);
     }
-    float o[kHd];
+    float o[32];
 #pragma unroll
-    for (int k = 0; k < kHd; ++k) o[k] = 0.f;
+    for (int k = 0; k < 32; ++k) o[k] = 0.f;
     float den = 0.f;
     if (mx != -INFINITY) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
             const float e = __expf(s[j] - mx);
             den += e;
+            const float4* vr = reinterpret_cast<const float4*>(&sV[j][half * 36]);
 #pragma unroll
-            for (int k = 0; k < kHd; ++k) o[k] = fmaf(e, sV[w][j][k], o[k]);
+            for (int c = 0; c < 8; ++c) {
+                const float4 v4 = vr[c];
+                o[4 * c] = fmaf(e, v4.x, o[4 * c]);
+                o[4 * c + 1] = fmaf(e, v4.y, o[4 * c + 1]);
+                o[4 * c + 2] = fmaf(e, v4.z, o[4 * c + 2]);
+                o[4 * c + 3] = fmaf(e, v4.w, o[4 * c + 3]);
+            }
         }
     }
     const float inv = den > 0.f ? 1.0f / den : 0.f;
-    __half* out = ctx + row * D + h * kHd;
+    __half* out = ctx + row * D + h * kHd + half * 32;
 #pragma unroll
-    for (int g = 0; g < kHd / 8; ++g) {
+    for (int g = 0; g < 4; ++g) {
         uint4 u;
         __half2* hh = reinterpret_cast<__half2*>(&u);
 #pragma unroll
@@ -419,34 +499,49 @@ int enc_make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, i
 
 using namespace ragrt;
 
+template <int BN>
+static int enc_gemm_launch(const void* d_A, const void* d_W, int32_t M, int32_t N, int32_t K, const EncGemmParams& p,
+                           cudaStream_t stream) {
+    CUtensorMap tA, tW;
+    int rc = enc_make_map(&tA, d_A, M, K, kEM);
+    if (rc || (rc = enc_make_map(&tW, d_W, N, K, BN))) return rc;
+    static bool attr = false;
+    if (!attr) {
+        RAGRT_CUDA_TRY(cudaFuncSetAttribute(enc_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            EncCfg<BN>::kSmem));
+        attr = true;
+    }
+    const int tiles = (N / BN) * (int)ceil_div(M, kEM);
+    enc_gemm<BN><<<(unsigned)std::min(tiles, num_sms()), kEThreads, EncCfg<BN>::kSmem, stream>>>(tA, tW, p);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
+}
+
 extern "C" int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual, void* d_out,
                               int32_t M, int32_t N, int32_t K, int32_t epilogue, void* stream_) {
     cudaStream_t stream = (cudaStream_t)stream_;
     RAGRT_REQUIRE(d_A && d_W && d_out, "null argument");
-    RAGRT_REQUIRE(M >= 1 && N >= kEN && N % kEN == 0 && K >= kEK && K % kEK == 0,
-                  "enc_gemm needs M >= 1, N a multiple of %d and K a multiple of %d (M=%d N=%d K=%d)", kEN, kEK,
+    RAGRT_REQUIRE(M >= 1 && N >= 128 && N % 128 == 0 && K >= kEK && K % kEK == 0,
+                  "enc_gemm needs M >= 1, N a multiple of 128 and K a multiple of %d (M=%d N=%d K=%d)", kEK,
                   (int)M, (int)N, (int)K);
     RAGRT_REQUIRE(epilogue >= kEpiBias && epilogue <= kEpiNorm, "unknown epilogue %d", (int)epilogue);
-    RAGRT_REQUIRE(epilogue != kEpiNorm || N == kEN, "the normalising epilogue needs N == %d", kEN);
+    RAGRT_REQUIRE(epilogue != kEpiNorm || N == 128, "the normalising epilogue needs N == 128");
     RAGRT_REQUIRE(epilogue != kEpiBiasResidual || d_residual, "the residual epilogue needs a residual");
     RAGRT_REQUIRE(((uintptr_t)d_A & 15) == 0 && ((uintptr_t)d_W & 15) == 0 && ((uintptr_t)d_out & 15) == 0 &&
                       ((uintptr_t)d_bias & 15) == 0 && ((uintptr_t)d_residual & 15) == 0,
                   "enc_gemm operands must be 16-byte aligned");
     int* err = device_error_flag();
     if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
-    CUtensorMap tA, tW;
-    int rc = enc_make_map(&tA, d_A, M, K, kEM);
-    if (rc || (rc = enc_make_map(&tW, d_W, N, K, kEN))) return rc;
-    static bool attr = false;
-    if (!attr) {
-        RAGRT_CUDA_TRY(cudaFuncSetAttribute(enc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kESmem));
-        attr = true;
-    }
     EncGemmParams p{M, N, K, epilogue, (const __half*)d_bias, (const __half*)d_residual, (__half*)d_out, err};
-    dim3 grid((unsigned)(N / kEN), (unsigned)ceil_div(M, kEM));
-    enc_gemm<<<grid, kEThreads, kESmem, stream>>>(tA, tW, p);
-    RAGRT_LAUNCH_CHECK();
-    return RAGRT_OK;
+    // 128 x 256 tiles (half the W re-reads per flop) unless 128 x 128 tiles fill the persistent
+    // CTAs' last round clearly better: the fraction of CTA rounds that hold a tile
+    const int sms = num_sms();
+    auto fill = [&](int bn) {
+        const int64_t t = (int64_t)(N / bn) * ceil_div(M, kEM);
+        return (double)t / (double)(ceil_div(t, (int64_t)sms) * sms);
+    };
+    const bool wide = epilogue != kEpiNorm && N % 256 == 0 && fill(256) >= fill(128) - 0.05;
+    return wide ? enc_gemm_launch<256>(d_A, d_W, M, N, K, p, stream) : enc_gemm_launch<128>(d_A, d_W, M, N, K, p, stream);
 }
 
 extern "C" int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const void* d_beta, float eps, void* d_out,
@@ -485,9 +580,9 @@ extern "C" int ragrt_enc_attention(const void* d_qkv, const int64_t* d_mask, voi
     RAGRT_REQUIRE(heads >= 1 && dim == heads * kHd, "enc_attention needs head_dim %d (dim %d, heads %d)", kHd,
                   (int)dim, (int)heads);
     RAGRT_REQUIRE(B >= 1, "B must be >= 1");
-    const int items = B * heads;
-    enc_attention<<<(unsigned)ceil_div(items, kAttWarps), kAttWarps * 32, 0, (cudaStream_t)stream_>>>(
-        (const __half*)d_qkv, d_mask, (__half*)d_ctx, B, heads, dim, 1.0f / sqrtf((float)kHd));
+    enc_attention<<<(unsigned)(B * heads), 64, 0, (cudaStream_t)stream_>>>((const __half*)d_qkv, d_mask,
+                                                                          (__half*)d_ctx, B, heads, dim,
+                                                                          1.0f / sqrtf((float)kHd));
     RAGRT_LAUNCH_CHECK();
     return RAGRT_OK;
 }

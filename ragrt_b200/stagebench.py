@@ -38,9 +38,75 @@ def timed(fn, steps, warmup):
     return e0.elapsed_time(e1) / steps
 
 
+def random_bert_weights(seed=0, layers=12, D=768, F_=3072, heads=12, vocab=30522, dim=128):
+    """BERT-base shaped fp16 weights in the layout of encoder.flat_weights (random: there is no
+    checkpoint offline; the speed does not depend on the values)."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    r = lambda *sh: (torch.randn(*sh, generator=g, device="cuda") * 0.02).half()
+    ln = lambda: (torch.ones(D, device="cuda").half(), torch.zeros(D, device="cuda").half())
+    W = {"emb_word": r(vocab, D), "emb_pos": r(512, D), "emb_type": r(D), "emb_ln": ln(), "heads": heads,
+         "eps": 1e-12, "act": "gelu", "linear": r(dim, D), "layers": []}
+    for _ in range(layers):
+        W["layers"].append({"qkv_w": r(3 * D, D), "qkv_b": r(3 * D), "o_w": r(D, D), "o_b": r(D), "ln1": ln(),
+                            "i_w": r(F_, D), "i_b": r(F_), "f_w": r(D, F_), "f_b": r(D), "ln2": ln()})
+    return W
+
+
+def torch_forward(W, ids, mask):
+    """The same network with torch operations (cuBLAS fp16 GEMMs, PyTorch's fused attention,
+    LayerNorm, GELU): the computation of the reference's torch encoder, timed beside ours."""
+    import torch.nn.functional as F
+    B, L = ids.shape
+    H = W["heads"]
+    x = W["emb_word"][ids] + W["emb_pos"][:L][None] + W["emb_type"]
+    D = x.shape[-1]
+    x = F.layer_norm(x, (D,), *W["emb_ln"], eps=W["eps"])
+    bias = (1.0 - mask[:, None, None, :].to(x.dtype)) * torch.finfo(x.dtype).min
+    for lw in W["layers"]:
+        qkv = F.linear(x, lw["qkv_w"], lw["qkv_b"]).view(B, L, 3, H, D // H).permute(2, 0, 3, 1, 4)
+        c = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2], attn_mask=bias).transpose(1, 2).reshape(B, L, D)
+        x = F.layer_norm(x + F.linear(c, lw["o_w"], lw["o_b"]), (D,), *lw["ln1"], eps=W["eps"])
+        h = F.gelu(F.linear(x, lw["i_w"], lw["i_b"]))
+        x = F.layer_norm(x + F.linear(h, lw["f_w"], lw["f_b"]), (D,), *lw["ln2"], eps=W["eps"])
+    return F.normalize(F.linear(x, W["linear"]).float(), p=2, dim=-1).half()
+
+
+def _graphed(fn, *args):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s), torch.no_grad():
+        for _ in range(2):
+            fn(*args)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g), torch.no_grad():
+        fn(*args)
+    return g
+
+
+def encode_stage(B, steps, warmup):
+    """Stage 0a: B queries x 32 tokens through BERT-base + ColBERT's linear, as one CUDA graph
+    of this build's kernels, and the same network in torch (cuBLAS + SDPA) as one graph."""
+    from .encoder import flat_forward
+    W = random_bert_weights()
+    g = torch.Generator(device="cuda").manual_seed(1)
+    ids = torch.randint(1000, 30000, (B, 32), generator=g, device="cuda")
+    mask = torch.ones(B, 32, dtype=torch.int64, device="cuda")
+    mask[:, 24:] = 0
+    ours = _graphed(flat_forward, W, ids, mask)
+    ref = _graphed(torch_forward, W, ids, mask)
+    ms = timed(ours.replay, steps, warmup)
+    ms_ref = timed(ref.replay, steps, warmup)
+    D, F_, layers = 768, 3072, 12
+    per_tok = layers * (2 * D * (3 * D + D + F_) + 2 * F_ * D + 4 * 32 * D) + 2 * D * 128
+    flops = per_tok * B * 32.0
+    return {"stage": "encode", "batch": B, "ms": ms, "queries_per_s": B / ms * 1e3, "tflops": flops / ms / 1e9,
+            "torch_ms": ms_ref, "torch_queries_per_s": B / ms_ref * 1e3, "work_gflop": flops / 1e9}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--stage", default="all", choices=("s2", "s3", "s4", "exact", "all"))
+    ap.add_argument("--stage", default="all", choices=("s2", "s3", "s4", "exact", "encode", "all"))
     ap.add_argument("--docs", type=int, default=2_000_000)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--nc", type=int, default=32)
@@ -95,6 +161,8 @@ def main():
         b = 256.0 * toks + 16.0 * pids.numel()
         out.append({"stage": "exact", "ms": ms, "gbs": b / ms / 1e6, "doc_tokens_per_s": toks / ms * 1e3,
                     "tflops": 2.0 * 32 * 128 * toks / ms / 1e9, "doc_tokens": toks})
+    if a.stage == "encode":
+        out.append(encode_stage(a.batch, a.steps, a.warmup))
     for o in out:
         print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in o.items()}), flush=True)
 
