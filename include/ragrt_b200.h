@@ -259,9 +259,12 @@ int ragrt_selftest_wait_timeout(uint32_t polls, void* stream);
  *   epilogue 4: fp16 rounding, then each row divided by its L2 norm (ColBERT linear + F.normalize,
  *               no bias; N must be 128)
  * N a multiple of 128, K a multiple of 64, all pointers 16-byte aligned; d_bias may be NULL.
+ * d_ws (ws_bytes, may be NULL / 0): scratch for small M, where the product is split along K
+ * over more CTAs and summed in fp32 by a second kernel (up to 148 x M x N x 4 bytes are used;
+ * fewer splits when the workspace is smaller).
  */
 int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual, void* d_out,
-                   int32_t M, int32_t N, int32_t K, int32_t epilogue, void* stream);
+                   int32_t M, int32_t N, int32_t K, int32_t epilogue, void* d_ws, int64_t ws_bytes, void* stream);
 
 /* LayerNorm of d_x[rows, dim] (fp32 statistics) with d_gamma / d_beta [dim]; dim 768. */
 int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const void* d_beta, float eps, void* d_out,

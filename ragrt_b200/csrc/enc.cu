@@ -51,6 +51,8 @@ struct EncGemmParams {
     const __half* residual;   // [M, N] or null
     __half* out;              // [M, N]
     int* err;
+    int ksplit;               // > 1: each unit sums a slice of K into partial[slice][M][N] (fp32)
+    float* partial;
 };
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
@@ -83,6 +85,7 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
     const int nk = p.K / kEK;
     const int tiles_n = p.N / BN;
     const int tiles = tiles_n * (int)((p.M + kEM - 1) / kEM);
+    const int units = tiles * p.ksplit;             // unit u: tile u / ksplit, K slice u % ksplit
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -110,9 +113,11 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             int g = 0;                                   // k-chunk counter over all of this CTA's tiles
-            for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+            for (int u = blockIdx.x; u < units && !failed; u += gridDim.x) {
+                const int t = u / p.ksplit, ks = u % p.ksplit;
                 const int m0 = (t / tiles_n) * kEM, n0 = (t % tiles_n) * BN;
-                for (int i = 0; i < nk; ++i, ++g) {
+                const int k0 = nk * ks / p.ksplit, k1 = nk * (ks + 1) / p.ksplit;
+                for (int i = k0; i < k1; ++i, ++g) {
                     const int s = g % S;
                     if (g >= S && !tc::mbar_wait_or_abort(empty + s, ((g / S) - 1) & 1, abort, kEWaitLimit)) {
                         failed = true;
@@ -129,7 +134,9 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_f16_f32(kEM, BN);
             int g = 0, j = 0, issued_g = -1;
-            for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x, ++j) {
+            for (int u = blockIdx.x; u < units && !failed; u += gridDim.x, ++j) {
+                const int ks = u % p.ksplit;
+                const int k0 = nk * ks / p.ksplit, k1 = nk * (ks + 1) / p.ksplit;
                 const int b = j & 1;
                 if (j >= 2 && !tc::mbar_wait_or_abort(acce + b, ((j >> 1) - 1) & 1, abort, kEWaitLimit)) {
                     failed = true;
@@ -137,7 +144,7 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
                 }
                 tc::fence_after();
                 const uint32_t d = tbase + (uint32_t)(b * BN);
-                for (int i = 0; i < nk; ++i, ++g) {
+                for (int i = k0; i < k1; ++i, ++g) {
                     const int s = g % S;
                     if (!tc::mbar_wait_or_abort(full + s, (g / S) & 1, abort, kEWaitLimit)) {
                         failed = true;
@@ -148,7 +155,7 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
 #pragma unroll
                     for (int k = 0; k < kEK / 16; ++k)
                         tc::mma_ss(d, tc::sw128_kmajor_desc(a + 32 * k), tc::sw128_kmajor_desc(bb + 32 * k), idesc,
-                                   (i | k) != 0);
+                                   (i != k0 || k != 0) ? 1u : 0u);
                     tc::mma_commit(empty + s);
                     issued_g = g;
                 }
@@ -161,7 +168,8 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
         // ------------------------------------------------------------ epilogue
         const int quad = warp & 3;
         int j = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+            const int t = u / p.ksplit, ks = u % p.ksplit;
             const int b = j & 1;
             const int m0 = (t / tiles_n) * kEM, n0 = (t % tiles_n) * BN;
             const int row = m0 + quad * 32 + lane;
@@ -172,7 +180,21 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
             }
             tc::fence_after();
             const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * BN);
-            if (p.epi == kEpiNorm) {
+            if (p.ksplit > 1) {
+                // this K slice's fp32 partial sums; enc_splitk_reduce applies the epilogue
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    tc::ld32x32(taddr + 32 * c, r);
+                    tc::wait_ld();
+                    if (row < p.M) {
+                        float* o = p.partial + ((int64_t)ks * p.M + row) * p.N + n0 + 32 * c;
+#pragma unroll
+                        for (int q = 0; q < 32; q += 4)
+                            *reinterpret_cast<uint4*>(o + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
+                    }
+                }
+            } else if (p.epi == kEpiNorm) {
                 // the whole 128-wide row is in this thread: fp16 rounding, then L2 norm in fp32
                 float v[128];
 #pragma unroll
@@ -261,6 +283,76 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
         tc::fence_after();
         tc::tmem_dealloc(tbase, Cfg::kTmemCols);
     }
+}
+
+// Sum of the K-slice partials of a split GEMM + the epilogue.  Elementwise epilogues: a thread
+// per 8 columns; the normalising one: a warp per 128-wide row.
+__global__ void enc_splitk_reduce(const float* __restrict__ partial, int ksplit, int M, int N, int epi,
+                                  const __half* __restrict__ bias, const __half* __restrict__ residual,
+                                  __half* __restrict__ out) {
+    if (epi == kEpiNorm) {
+        const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+        if (row >= M) return;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s = 0; s < ksplit; ++s) {
+            const float4 f = *reinterpret_cast<const float4*>(partial + ((int64_t)s * M + row) * N + 4 * lane);
+            v[0] += f.x; v[1] += f.y; v[2] += f.z; v[3] += f.w;
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            v[e] = __half2float(__float2half_rn(v[e]));
+            ss = fmaf(v[e], v[e], ss);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+        __half2* o2 = reinterpret_cast<__half2*>(out + (int64_t)row * N + 4 * lane);
+        o2[0] = __floats2half2_rn(v[0] * inv, v[1] * inv);
+        o2[1] = __floats2half2_rn(v[2] * inv, v[3] * inv);
+        return;
+    }
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;     // group of 8 columns
+    if (g >= (int64_t)M * (N / 8)) return;
+    const int row = (int)(g / (N / 8)), col = (int)(g % (N / 8)) * 8;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < ksplit; ++s) {
+        const float* src = partial + ((int64_t)s * M + row) * N + col;
+        const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
+        f[0] += a.x; f[1] += a.y; f[2] += a.z; f[3] += a.w;
+        f[4] += b.x; f[5] += b.y; f[6] += b.z; f[7] += b.w;
+    }
+    if (bias) {
+        const uint4 bu = __ldg(reinterpret_cast<const uint4*>(bias + col));
+        const __half2* bh = reinterpret_cast<const __half2*>(&bu);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 b2 = __half22float2(bh[e]);
+            f[2 * e] += b2.x;
+            f[2 * e + 1] += b2.y;
+        }
+    }
+    if (epi == kEpiBiasGelu) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = gelu_erf(f[e]);
+    } else if (epi == kEpiBiasGeluTanh) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = gelu_tanh(f[e]);
+    } else if (epi == kEpiBiasResidual) {
+        const uint4 ru = *reinterpret_cast<const uint4*>(residual + (int64_t)row * N + col);
+        const __half2* rh = reinterpret_cast<const __half2*>(&ru);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 r2 = __half22float2(rh[e]);
+            f[2 * e] += r2.x;
+            f[2 * e + 1] += r2.y;
+        }
+    }
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
+    *reinterpret_cast<uint4*>(out + (int64_t)row * N + col) = u;
 }
 
 // LayerNorm of one row held by a warp: 8 fp16 per lane per 256 columns.
@@ -511,14 +603,15 @@ static int enc_gemm_launch(const void* d_A, const void* d_W, int32_t M, int32_t 
                                             EncCfg<BN>::kSmem));
         attr = true;
     }
-    const int tiles = (N / BN) * (int)ceil_div(M, kEM);
-    enc_gemm<BN><<<(unsigned)std::min(tiles, num_sms()), kEThreads, EncCfg<BN>::kSmem, stream>>>(tA, tW, p);
+    const int units = (N / BN) * (int)ceil_div(M, kEM) * p.ksplit;
+    enc_gemm<BN><<<(unsigned)std::min(units, num_sms()), kEThreads, EncCfg<BN>::kSmem, stream>>>(tA, tW, p);
     RAGRT_LAUNCH_CHECK();
     return RAGRT_OK;
 }
 
 extern "C" int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual, void* d_out,
-                              int32_t M, int32_t N, int32_t K, int32_t epilogue, void* stream_) {
+                              int32_t M, int32_t N, int32_t K, int32_t epilogue, void* d_ws, int64_t ws_bytes,
+                              void* stream_) {
     cudaStream_t stream = (cudaStream_t)stream_;
     RAGRT_REQUIRE(d_A && d_W && d_out, "null argument");
     RAGRT_REQUIRE(M >= 1 && N >= 128 && N % 128 == 0 && K >= kEK && K % kEK == 0,
@@ -528,20 +621,43 @@ extern "C" int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bi
     RAGRT_REQUIRE(epilogue != kEpiNorm || N == 128, "the normalising epilogue needs N == 128");
     RAGRT_REQUIRE(epilogue != kEpiBiasResidual || d_residual, "the residual epilogue needs a residual");
     RAGRT_REQUIRE(((uintptr_t)d_A & 15) == 0 && ((uintptr_t)d_W & 15) == 0 && ((uintptr_t)d_out & 15) == 0 &&
-                      ((uintptr_t)d_bias & 15) == 0 && ((uintptr_t)d_residual & 15) == 0,
+                      ((uintptr_t)d_bias & 15) == 0 && ((uintptr_t)d_residual & 15) == 0 &&
+                      ((uintptr_t)d_ws & 15) == 0,
                   "enc_gemm operands must be 16-byte aligned");
     int* err = device_error_flag();
     if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
-    EncGemmParams p{M, N, K, epilogue, (const __half*)d_bias, (const __half*)d_residual, (__half*)d_out, err};
-    // 128 x 256 tiles (half the W re-reads per flop) unless 128 x 128 tiles fill the persistent
-    // CTAs' last round clearly better: the fraction of CTA rounds that hold a tile
+    EncGemmParams p{M, N, K, epilogue, (const __half*)d_bias, (const __half*)d_residual, (__half*)d_out, err, 1,
+                    nullptr};
     const int sms = num_sms();
+    const int64_t mt = ceil_div(M, kEM);
+    // tiles of 128 x 256 (half the W re-reads per flop) when they fill the GPU and their last
+    // round of persistent CTAs is about as full as with 128 x 128 tiles; else 128 x 128
     auto fill = [&](int bn) {
-        const int64_t t = (int64_t)(N / bn) * ceil_div(M, kEM);
+        const int64_t t = (int64_t)(N / bn) * mt;
         return (double)t / (double)(ceil_div(t, (int64_t)sms) * sms);
     };
-    const bool wide = epilogue != kEpiNorm && N % 256 == 0 && fill(256) >= fill(128) - 0.05;
-    return wide ? enc_gemm_launch<256>(d_A, d_W, M, N, K, p, stream) : enc_gemm_launch<128>(d_A, d_W, M, N, K, p, stream);
+    const bool wide = epilogue != kEpiNorm && N % 256 == 0 && (N / 256) * mt >= sms && fill(256) >= fill(128) - 0.05;
+    const int bn = wide ? 256 : 128;
+    const int64_t tiles = (N / bn) * mt;
+    // too few tiles to occupy the SMs (small batches): split K across CTAs, fp32 partials in
+    // the caller's workspace, then one reduction that applies the epilogue
+    if (tiles * 2 <= sms) {
+        int64_t ks = std::min<int64_t>(K / kEK, sms / tiles);
+        const int64_t per = (int64_t)M * N * 4;
+        ks = std::min<int64_t>(ks, d_ws ? ws_bytes / per : 0);
+        if (ks > 1) {
+            p.ksplit = (int)ks;
+            p.partial = (float*)d_ws;
+        }
+    }
+    int rc = wide ? enc_gemm_launch<256>(d_A, d_W, M, N, K, p, stream) : enc_gemm_launch<128>(d_A, d_W, M, N, K, p, stream);
+    if (rc || p.ksplit == 1) return rc;
+    const int threads = 256;
+    const int64_t work = epilogue == kEpiNorm ? (int64_t)M * 32 : (int64_t)M * (N / 8);
+    enc_splitk_reduce<<<(unsigned)ceil_div(work, (int64_t)threads), threads, 0, stream>>>(
+        p.partial, p.ksplit, M, N, epilogue, (const __half*)d_bias, (const __half*)d_residual, (__half*)d_out);
+    RAGRT_LAUNCH_CHECK();
+    return RAGRT_OK;
 }
 
 extern "C" int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const void* d_beta, float eps, void* d_out,

@@ -66,12 +66,21 @@ def flat_weights(bert, linear, dtype=torch.float16, device="cuda"):
     return W
 
 
-def _gemm(a, w, bias, out, epi, residual=None):
+def _gemm(a, w, bias, out, epi, residual=None, ws=None):
     M, K = a.shape
     N = w.shape[0]
+    nbytes = ws.numel() * ws.element_size() if ws is not None else 0
     _lib.check(_lib.lib().ragrt_enc_gemm(_ptr(a), _ptr(w), _ptr(bias), _ptr(residual), _ptr(out), M, N, K, epi,
-                                         _stream()))
+                                         _ptr(ws), nbytes, _stream()))
     return out
+
+
+def _split_workspace(device):
+    """Scratch for the K-split products of small batches.  A product is split only while its
+    128 x 128 tiles number at most half the SMs, into at most SMs / tiles slices, so the fp32
+    partials never exceed SMs x 128 x 128 values (9.7 MB on 148 SMs)."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    return torch.empty(sms * 128 * 128, dtype=torch.float32, device=device)
 
 
 def _layernorm(x, ln, eps, out):
@@ -100,20 +109,21 @@ def flat_forward(W, ids, mask):
     ctx = torch.empty(M, D, dtype=torch.float16, device=dev)
     qkv = torch.empty(M, 3 * D, dtype=torch.float16, device=dev)
     h = torch.empty(M, W["layers"][0]["i_w"].shape[0], dtype=torch.float16, device=dev)
+    ws = _split_workspace(dev)
     _lib.check(_lib.lib().ragrt_enc_embed(_ptr(ids), _ptr(W["emb_word"]), _ptr(W["emb_pos"]), _ptr(W["emb_type"]),
                                           _ptr(W["emb_ln"][0]), _ptr(W["emb_ln"][1]), float(eps),
                                           W["emb_word"].shape[0], B, L, D, _ptr(x), _stream()))
     gelu = EPI_BIAS_GELU_TANH if W["act"] in ("gelu_new", "gelu_pytorch_tanh") else EPI_BIAS_GELU
     for lw in W["layers"]:
-        _gemm(x, lw["qkv_w"], lw["qkv_b"], qkv, EPI_BIAS)
+        _gemm(x, lw["qkv_w"], lw["qkv_b"], qkv, EPI_BIAS, ws=ws)
         _lib.check(_lib.lib().ragrt_enc_attention(_ptr(qkv), _ptr(mask), _ptr(ctx), B, L, H, D, _stream()))
-        _gemm(ctx, lw["o_w"], lw["o_b"], y, EPI_BIAS_RESIDUAL, residual=x)
+        _gemm(ctx, lw["o_w"], lw["o_b"], y, EPI_BIAS_RESIDUAL, residual=x, ws=ws)
         _layernorm(y, lw["ln1"], eps, x)
-        _gemm(x, lw["i_w"], lw["i_b"], h, gelu)
-        _gemm(h, lw["f_w"], lw["f_b"], y, EPI_BIAS_RESIDUAL, residual=x)
+        _gemm(x, lw["i_w"], lw["i_b"], h, gelu, ws=ws)
+        _gemm(h, lw["f_w"], lw["f_b"], y, EPI_BIAS_RESIDUAL, residual=x, ws=ws)
         _layernorm(y, lw["ln2"], eps, x)
     out = torch.empty(M, W["linear"].shape[0], dtype=torch.float16, device=dev)
-    _gemm(x, W["linear"], None, out, EPI_NORM)
+    _gemm(x, W["linear"], None, out, EPI_NORM, ws=ws)
     return out.view(B, L, -1)
 
 

@@ -44,6 +44,31 @@ def test_gemm_epilogues(M, epi):
     assert err.max().item() <= 2e-3 * ref.abs().max().item() + 2e-3, err.max().item()
 
 
+@pytest.mark.parametrize("M,N,K", [(32, 768, 3072), (32, 3072, 768), (200, 768, 768), (64, 128, 768)])
+@pytest.mark.parametrize("epi", [encoder.EPI_BIAS_GELU, encoder.EPI_BIAS_RESIDUAL, encoder.EPI_NORM])
+def test_gemm_split_k_equals_reference(M, N, K, epi):
+    """Small M: the product is split along K over more CTAs and summed in fp32 by a second
+    kernel that applies the epilogue."""
+    if epi == encoder.EPI_NORM and N != 128:
+        pytest.skip("the normalising epilogue is for the 128-wide projection")
+    g = torch.Generator(device="cuda").manual_seed(M * 3 + N + epi)
+    a = torch.randn(M, K, generator=g, device="cuda").half()
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.05).half()
+    b = None if epi == encoder.EPI_NORM else (torch.randn(N, generator=g, device="cuda") * 0.1).half()
+    r = torch.randn(M, N, generator=g, device="cuda").half()
+    ws = encoder._split_workspace(torch.device("cuda"))
+    out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    got = encoder._gemm(a, w, b, out, epi, residual=r if epi == encoder.EPI_BIAS_RESIDUAL else None, ws=ws).float()
+    ref = a.float() @ w.float().t()
+    if epi == encoder.EPI_NORM:
+        ref = F.normalize(ref.half().float(), dim=-1)
+    else:
+        ref = ref + b.float()
+        ref = F.gelu(ref) if epi == encoder.EPI_BIAS_GELU else ref + r.float()
+    err = (got - ref).abs().max().item()
+    assert err <= 2e-3 * ref.abs().max().item() + 2e-3, err
+
+
 def test_gemm_norm_epilogue():
     g = torch.Generator(device="cuda").manual_seed(3)
     a = torch.randn(160, 768, generator=g, device="cuda").half()
