@@ -266,6 +266,17 @@ int ragrt_selftest_wait_timeout(uint32_t polls, void* stream);
 int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual, void* d_out,
                    int32_t M, int32_t N, int32_t K, int32_t epilogue, void* d_ws, int64_t ws_bytes, void* stream);
 
+/*
+ * d_out = LayerNorm(d_A . d_W^T + d_bias + d_residual) with d_gamma / d_beta, N = 768: the
+ * attention-output and output-dense blocks (fast_encoder.py:73, :76).  When the product is
+ * split along K (small M, workspace d_ws as for ragrt_enc_gemm) the partial sums are reduced
+ * straight into the LayerNorm; otherwise the product goes through d_tmp [M, N] and the
+ * LayerNorm kernel.  d_out may be d_residual.
+ */
+int ragrt_enc_gemm_residual_ln(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual,
+                               const void* d_gamma, const void* d_beta, float eps, void* d_tmp, void* d_out,
+                               int32_t M, int32_t N, int32_t K, void* d_ws, int64_t ws_bytes, void* stream);
+
 /* LayerNorm of d_x[rows, dim] (fp32 statistics) with d_gamma / d_beta [dim]; dim 768. */
 int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const void* d_beta, float eps, void* d_out,
                         int32_t rows, int32_t dim, void* stream);

@@ -20,6 +20,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <utility>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -42,6 +43,15 @@ struct EncCfg {
     static constexpr int kSmem = 1024 + kStages * (kETileA + kTileB) + 256;
     static constexpr uint32_t kTmemCols = 2 * BN;       // two accumulator buffers
 };
+
+// Programmatic dependent launch: every encoder kernel is launched so that it may start while
+// its predecessor in the stream drains; it does its own set-up, then waits for the
+// predecessor's results (griddepcontrol.wait returns at once for a normal launch) and lets
+// its own successor start early.
+__device__ __forceinline__ void pdl_wait_then_release() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 enum EncEpilogue : int { kEpiBias = 0, kEpiBiasGelu = 1, kEpiBiasGeluTanh = 2, kEpiBiasResidual = 3, kEpiNorm = 4 };
 
@@ -108,6 +118,7 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
     tc::fence_after();
     const uint32_t tbase = *tslot;
     bool failed = false;
+    pdl_wait_then_release();
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -290,6 +301,7 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
 __global__ void enc_splitk_reduce(const float* __restrict__ partial, int ksplit, int M, int N, int epi,
                                   const __half* __restrict__ bias, const __half* __restrict__ residual,
                                   __half* __restrict__ out) {
+    pdl_wait_then_release();
     if (epi == kEpiNorm) {
         const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
         if (row >= M) return;
@@ -412,11 +424,72 @@ __device__ __forceinline__ void load_row(const __half* src, float (&v)[kDimT / 3
 template <int kDimT>
 __global__ void enc_layernorm(const __half* __restrict__ x, const __half* __restrict__ gamma,
                               const __half* __restrict__ beta, float eps, __half* __restrict__ out, int rows) {
+    pdl_wait_then_release();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     float v[kDimT / 32];
     load_row<kDimT>(x + (int64_t)warp * kDimT, v, lane);
     warp_layernorm_store<kDimT>(v, gamma, beta, eps, out + (int64_t)warp * kDimT, lane);
+}
+
+// out = LN(sum of the K-slice partials + bias + residual), a CTA of kDimT / 3 threads per row
+// (3 columns per thread, coalesced partial reads; mean and variance by block reduction).  A
+// CTA reads its residual row before writing its output row, so out may be the residual.
+template <int kDimT>
+__global__ void __launch_bounds__(kDimT / 3)
+enc_splitk_reduce_ln(const float* __restrict__ partial, int ksplit, int M, const __half* __restrict__ bias,
+                     const __half* residual, const __half* __restrict__ gamma, const __half* __restrict__ beta,
+                     float eps, __half* out) {
+    constexpr int kT = kDimT / 3, kW = kT / 32;
+    __shared__ float red[2][kW];
+    pdl_wait_then_release();
+    const int row = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
+    float v[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const int col = t + c * kT;
+        v[c] = __half2float(bias[col]) + __half2float(residual[(int64_t)row * kDimT + col]);
+    }
+    for (int s_ = 0; s_ < ksplit; ++s_) {
+        const float* src = partial + ((int64_t)s_ * M + row) * kDimT;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) v[c] += src[t + c * kT];
+    }
+    // the unfused path rounds the residual sum to fp16 before its LayerNorm: so does this one
+    float sum = 0.f;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        v[c] = __half2float(__float2half_rn(v[c]));
+        sum += v[c];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    if (lane == 0) red[0][w] = sum;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kW; ++i) tot += red[0][i];
+    const float mean = tot * (1.0f / kDimT);
+    float q = 0.f;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float d = v[c] - mean;
+        q = fmaf(d, d, q);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
+    if (lane == 0) red[1][w] = q;
+    __syncthreads();
+    float qt = 0.f;
+#pragma unroll
+    for (int i = 0; i < kW; ++i) qt += red[1][i];
+    const float rstd = rsqrtf(qt * (1.0f / kDimT) + eps);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const int col = t + c * kT;
+        out[(int64_t)row * kDimT + col] =
+            __float2half_rn((v[c] - mean) * rstd * __half2float(gamma[col]) + __half2float(beta[col]));
+    }
 }
 
 // x[row] = LN(word[ids[row]] + pos[row % L] + type), summed in fp32 (token ids outside the
@@ -426,6 +499,7 @@ __global__ void enc_embed_ln(const int64_t* __restrict__ ids, const __half* __re
                              const __half* __restrict__ pos, const __half* __restrict__ type,
                              const __half* __restrict__ gamma, const __half* __restrict__ beta, float eps, int vocab,
                              int L, int rows, __half* __restrict__ out, int* err) {
+    pdl_wait_then_release();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     int64_t id = ids[warp];
@@ -456,6 +530,7 @@ enc_attention(const __half* __restrict__ qkv, const int64_t* __restrict__ mask, 
               int H, int D, float scale) {
     __shared__ __align__(16) float sK[32][kKvStride];
     __shared__ __align__(16) float sV[32][kKvStride];
+    pdl_wait_then_release();
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int b = blockIdx.x / H, h = blockIdx.x % H;
     // stage K and V: thread t loads token t / 2, half t % 2 (32 dims = 4 x 16 B) of each
@@ -555,6 +630,28 @@ enc_attention(const __half* __restrict__ qkv, const int64_t* __restrict__ mask, 
     }
 }
 
+// Launch with programmatic stream serialisation (see pdl_wait_then_release).
+template <typename... KArgs, typename... Args>
+int enc_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(RAGRT_ERR_CUDA, "encoder kernel launch: %s", cudaGetErrorString(e));
+    }
+    count_launch();
+    return RAGRT_OK;
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -604,9 +701,8 @@ static int enc_gemm_launch(const void* d_A, const void* d_W, int32_t M, int32_t 
         attr = true;
     }
     const int units = (N / BN) * (int)ceil_div(M, kEM) * p.ksplit;
-    enc_gemm<BN><<<(unsigned)std::min(units, num_sms()), kEThreads, EncCfg<BN>::kSmem, stream>>>(tA, tW, p);
-    RAGRT_LAUNCH_CHECK();
-    return RAGRT_OK;
+    return enc_launch(enc_gemm<BN>, dim3((unsigned)std::min(units, num_sms())), dim3(kEThreads), EncCfg<BN>::kSmem,
+                      stream, tA, tW, p);
 }
 
 extern "C" int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual, void* d_out,
@@ -654,10 +750,47 @@ extern "C" int ragrt_enc_gemm(const void* d_A, const void* d_W, const void* d_bi
     if (rc || p.ksplit == 1) return rc;
     const int threads = 256;
     const int64_t work = epilogue == kEpiNorm ? (int64_t)M * 32 : (int64_t)M * (N / 8);
-    enc_splitk_reduce<<<(unsigned)ceil_div(work, (int64_t)threads), threads, 0, stream>>>(
-        p.partial, p.ksplit, M, N, epilogue, (const __half*)d_bias, (const __half*)d_residual, (__half*)d_out);
-    RAGRT_LAUNCH_CHECK();
-    return RAGRT_OK;
+    return enc_launch(enc_splitk_reduce, dim3((unsigned)ceil_div(work, (int64_t)threads)), dim3(threads), 0, stream,
+                      (const float*)p.partial, p.ksplit, (int)M, (int)N, (int)epilogue, (const __half*)d_bias,
+                      (const __half*)d_residual, (__half*)d_out);
+}
+
+extern "C" int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const void* d_beta, float eps, void* d_out,
+                                   int32_t rows, int32_t dim, void* stream_);
+
+extern "C" int ragrt_enc_gemm_residual_ln(const void* d_A, const void* d_W, const void* d_bias, const void* d_residual,
+                                          const void* d_gamma, const void* d_beta, float eps, void* d_tmp,
+                                          void* d_out, int32_t M, int32_t N, int32_t K, void* d_ws,
+                                          int64_t ws_bytes, void* stream_) {
+    cudaStream_t stream = (cudaStream_t)stream_;
+    RAGRT_REQUIRE(d_bias && d_residual && d_gamma && d_beta && d_tmp && d_out, "null argument");
+    RAGRT_REQUIRE(N == 768, "enc_gemm_residual_ln is built for N = 768 (BERT-base); got %d", (int)N);
+    // the split decision of ragrt_enc_gemm, with its partials reduced straight into the LayerNorm
+    const int sms = num_sms();
+    const int64_t tiles = (int64_t)(N / 128) * ceil_div(M, kEM);
+    int64_t ks = 1;
+    if (tiles * 2 <= sms && K % kEK == 0) {
+        ks = std::min<int64_t>(K / kEK, sms / tiles);
+        ks = std::min<int64_t>(ks, d_ws ? ws_bytes / ((int64_t)M * N * 4) : 0);
+    }
+    if (ks <= 1) {
+        int rc = ragrt_enc_gemm(d_A, d_W, d_bias, d_residual, d_tmp, M, N, K, kEpiBiasResidual, nullptr, 0, stream_);
+        if (rc) return rc;
+        return ragrt_enc_layernorm(d_tmp, d_gamma, d_beta, eps, d_out, M, N, stream_);
+    }
+    RAGRT_REQUIRE(M >= 1 && K >= kEK && K % kEK == 0, "enc_gemm needs K a multiple of %d", kEK);
+    RAGRT_REQUIRE(((uintptr_t)d_A & 15) == 0 && ((uintptr_t)d_W & 15) == 0 && ((uintptr_t)d_ws & 15) == 0 &&
+                      ((uintptr_t)d_residual & 15) == 0 && ((uintptr_t)d_out & 15) == 0,
+                  "enc_gemm operands must be 16-byte aligned");
+    int* err = device_error_flag();
+    if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
+    EncGemmParams p{M, N, K, kEpiBiasResidual, (const __half*)d_bias, (const __half*)d_residual, (__half*)d_tmp, err,
+                    (int)ks, (float*)d_ws};
+    int rc = enc_gemm_launch<128>(d_A, d_W, M, N, K, p, stream);
+    if (rc) return rc;
+    return enc_launch(enc_splitk_reduce_ln<768>, dim3((unsigned)M), dim3(768 / 3), 0, stream, (const float*)d_ws,
+                      (int)ks, (int)M, (const __half*)d_bias,
+                      (const __half*)d_residual, (const __half*)d_gamma, (const __half*)d_beta, eps, (__half*)d_out);
 }
 
 extern "C" int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const void* d_beta, float eps, void* d_out,
@@ -667,10 +800,9 @@ extern "C" int ragrt_enc_layernorm(const void* d_x, const void* d_gamma, const v
     RAGRT_REQUIRE(rows >= 0, "rows must be >= 0");
     if (rows == 0) return RAGRT_OK;
     const int threads = 256;
-    enc_layernorm<768><<<(unsigned)ceil_div((int64_t)rows * 32, threads), threads, 0, (cudaStream_t)stream_>>>(
-        (const __half*)d_x, (const __half*)d_gamma, (const __half*)d_beta, eps, (__half*)d_out, rows);
-    RAGRT_LAUNCH_CHECK();
-    return RAGRT_OK;
+    return enc_launch(enc_layernorm<768>, dim3((unsigned)ceil_div((int64_t)rows * 32, threads)), dim3(threads), 0,
+                      (cudaStream_t)stream_, (const __half*)d_x, (const __half*)d_gamma, (const __half*)d_beta, eps,
+                      (__half*)d_out, (int)rows);
 }
 
 extern "C" int ragrt_enc_embed(const int64_t* d_ids, const void* d_word, const void* d_pos, const void* d_type,
@@ -682,11 +814,10 @@ extern "C" int ragrt_enc_embed(const int64_t* d_ids, const void* d_word, const v
     int* err = device_error_flag();
     if (!err) return fail(RAGRT_ERR_CUDA, "device error flag unavailable");
     const int rows = B * L, threads = 256;
-    enc_embed_ln<768><<<(unsigned)ceil_div((int64_t)rows * 32, threads), threads, 0, (cudaStream_t)stream_>>>(
-        d_ids, (const __half*)d_word, (const __half*)d_pos, (const __half*)d_type, (const __half*)d_gamma,
-        (const __half*)d_beta, eps, vocab, L, rows, (__half*)d_out, err);
-    RAGRT_LAUNCH_CHECK();
-    return RAGRT_OK;
+    return enc_launch(enc_embed_ln<768>, dim3((unsigned)ceil_div((int64_t)rows * 32, threads)), dim3(threads), 0,
+                      (cudaStream_t)stream_, d_ids, (const __half*)d_word, (const __half*)d_pos, (const __half*)d_type,
+                      (const __half*)d_gamma, (const __half*)d_beta, eps, (int)vocab, (int)L, (int)rows,
+                      (__half*)d_out, err);
 }
 
 extern "C" int ragrt_enc_attention(const void* d_qkv, const int64_t* d_mask, void* d_ctx, int32_t B, int32_t L,
@@ -696,9 +827,7 @@ extern "C" int ragrt_enc_attention(const void* d_qkv, const int64_t* d_mask, voi
     RAGRT_REQUIRE(heads >= 1 && dim == heads * kHd, "enc_attention needs head_dim %d (dim %d, heads %d)", kHd,
                   (int)dim, (int)heads);
     RAGRT_REQUIRE(B >= 1, "B must be >= 1");
-    enc_attention<<<(unsigned)(B * heads), 64, 0, (cudaStream_t)stream_>>>((const __half*)d_qkv, d_mask,
-                                                                          (__half*)d_ctx, B, heads, dim,
-                                                                          1.0f / sqrtf((float)kHd));
-    RAGRT_LAUNCH_CHECK();
-    return RAGRT_OK;
+    return enc_launch(enc_attention, dim3((unsigned)(B * heads)), dim3(64), 0, (cudaStream_t)stream_,
+                      (const __half*)d_qkv, d_mask, (__half*)d_ctx, (int)B, (int)heads, (int)dim,
+                      1.0f / sqrtf((float)kHd));
 }

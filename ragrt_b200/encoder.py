@@ -83,6 +83,16 @@ def _split_workspace(device):
     return torch.empty(sms * 128 * 128, dtype=torch.float32, device=device)
 
 
+def _gemm_residual_ln(a, w, bias, residual, ln, eps, tmp, out, ws=None):
+    M, K = a.shape
+    N = w.shape[0]
+    nbytes = ws.numel() * ws.element_size() if ws is not None else 0
+    _lib.check(_lib.lib().ragrt_enc_gemm_residual_ln(_ptr(a), _ptr(w), _ptr(bias), _ptr(residual), _ptr(ln[0]),
+                                                     _ptr(ln[1]), float(eps), _ptr(tmp), _ptr(out), M, N, K,
+                                                     _ptr(ws), nbytes, _stream()))
+    return out
+
+
 def _layernorm(x, ln, eps, out):
     _lib.check(_lib.lib().ragrt_enc_layernorm(_ptr(x), _ptr(ln[0]), _ptr(ln[1]), float(eps), _ptr(out), x.shape[0],
                                               x.shape[1], _stream()))
@@ -117,11 +127,9 @@ def flat_forward(W, ids, mask):
     for lw in W["layers"]:
         _gemm(x, lw["qkv_w"], lw["qkv_b"], qkv, EPI_BIAS, ws=ws)
         _lib.check(_lib.lib().ragrt_enc_attention(_ptr(qkv), _ptr(mask), _ptr(ctx), B, L, H, D, _stream()))
-        _gemm(ctx, lw["o_w"], lw["o_b"], y, EPI_BIAS_RESIDUAL, residual=x, ws=ws)
-        _layernorm(y, lw["ln1"], eps, x)
+        _gemm_residual_ln(ctx, lw["o_w"], lw["o_b"], x, lw["ln1"], eps, y, x, ws=ws)
         _gemm(x, lw["i_w"], lw["i_b"], h, gelu, ws=ws)
-        _gemm(h, lw["f_w"], lw["f_b"], y, EPI_BIAS_RESIDUAL, residual=x, ws=ws)
-        _layernorm(y, lw["ln2"], eps, x)
+        _gemm_residual_ln(h, lw["f_w"], lw["f_b"], x, lw["ln2"], eps, y, x, ws=ws)
     out = torch.empty(M, W["linear"].shape[0], dtype=torch.float16, device=dev)
     _gemm(x, W["linear"], None, out, EPI_NORM, ws=ws)
     return out.view(B, L, -1)

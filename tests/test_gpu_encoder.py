@@ -69,6 +69,26 @@ def test_gemm_split_k_equals_reference(M, N, K, epi):
     assert err <= 2e-3 * ref.abs().max().item() + 2e-3, err
 
 
+@pytest.mark.parametrize("M,K", [(64, 768), (32, 3072), (4096, 768)])
+def test_gemm_residual_layernorm(M, K):
+    """LN(A W^T + b + residual) written over the residual: split K with the LayerNorm fused into
+    the reduction (small M), or the residual epilogue then the LayerNorm kernel (large M)."""
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    N = 768
+    a = torch.randn(M, K, generator=g, device="cuda").half()
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.03).half()
+    b = (torch.randn(N, generator=g, device="cuda") * 0.1).half()
+    x = torch.randn(M, N, generator=g, device="cuda").half()
+    gamma = (1 + 0.1 * torch.randn(N, generator=g, device="cuda")).half()
+    beta = (0.1 * torch.randn(N, generator=g, device="cuda")).half()
+    ref = F.layer_norm((a.float() @ w.float().t() + b.float() + x.float()).half().float(), (N,), gamma.float(),
+                       beta.float(), eps=1e-12)
+    tmp = torch.empty_like(x)
+    ws = encoder._split_workspace(torch.device("cuda"))
+    got = encoder._gemm_residual_ln(a, w, b, x, (gamma, beta), 1e-12, tmp, x, ws=ws).float()
+    assert (got - ref).abs().max().item() < 2e-2
+
+
 def test_gemm_norm_epilogue():
     g = torch.Generator(device="cuda").manual_seed(3)
     a = torch.randn(160, 768, generator=g, device="cuda").half()
