@@ -11,7 +11,8 @@
 //                  (128-byte swizzle, K-major, no multicast).  Fused epilogues: + bias,
 //                  gelu (erf or tanh form), + residual, or the final fp16 rounding + L2
 //                  normalisation of a 128-wide row.  Warp 0 issues the TMA loads, warp 1 the
-//                  MMAs, warps 2-5 drain the accumulator (one 32-row quadrant each).
+//                  MMAs, warps 2-9 drain the accumulator (two per 32-row quadrant, each
+//                  taking half of the tile's columns).
 //   enc_embed_ln   embedding sum + LayerNorm, a warp per token row.
 //   enc_layernorm  LayerNorm of a [rows, dim] fp16 matrix, a warp per row (fp32 statistics).
 //   enc_attention  two warps per (query, head): 32 tokens x head_dim 64; scores, masked
@@ -32,7 +33,7 @@ namespace {
 constexpr int kEM = 128;                 // rows per tile (MMA M)
 constexpr int kEK = 64;                  // K per stage: one 128-byte swizzle atom of fp16
 constexpr int kETileA = kEM * kEK * 2;   // 16 KB
-constexpr int kEThreads = 192;           // 6 warps
+constexpr int kEThreads = 320;           // 10 warps: TMA, MMA, 8 epilogue
 constexpr uint32_t kEWaitLimit = 1u << 26;
 constexpr int kEStageBudget = 192 * 1024;
 
@@ -104,7 +105,7 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(accf + b, 1);
-            tc::mbar_init(acce + b, 4);
+            tc::mbar_init(acce + b, 8);
         }
         *abort = 0;
         tc::mbar_fence_init();
@@ -177,7 +178,9 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int quad = warp & 3;
+        const int quad = warp & 3;                  // tensor-memory lane quadrant of this warp
+        const int half = (warp - 2) >> 2;          // which half of the tile's columns
+        const int c0 = half * (BN / 64), c1 = c0 + BN / 64;
         int j = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
             const int t = u / p.ksplit, ks = u % p.ksplit;
@@ -194,7 +197,7 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
             if (p.ksplit > 1) {
                 // this K slice's fp32 partial sums; enc_splitk_reduce applies the epilogue
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
+                for (int c = c0; c < c1; ++c) {
                     uint32_t r[32];
                     tc::ld32x32(taddr + 32 * c, r);
                     tc::wait_ld();
@@ -206,7 +209,9 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
                     }
                 }
             } else if (p.epi == kEpiNorm) {
-                // the whole 128-wide row is in this thread: fp16 rounding, then L2 norm in fp32
+                // the whole 128-wide row is in one thread (of the first half's warps): fp16
+                // rounding, then L2 norm in fp32
+                if (half == 0) {
                 float v[128];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -231,9 +236,10 @@ enc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtens
                         *reinterpret_cast<uint4*>(o + q) = u;
                     }
                 }
+                }
             } else {
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
+                for (int c = c0; c < c1; ++c) {
                     uint32_t r[32];
                     tc::ld32x32(taddr + 32 * c, r);
                     tc::wait_ld();
