@@ -21,6 +21,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <utility>
 
 #include "common.cuh"
@@ -700,11 +701,15 @@ static int enc_gemm_launch(const void* d_A, const void* d_W, int32_t M, int32_t 
     CUtensorMap tA, tW;
     int rc = enc_make_map(&tA, d_A, M, K, kEM);
     if (rc || (rc = enc_make_map(&tW, d_W, N, K, BN))) return rc;
-    static bool attr = false;
-    if (!attr) {
+    // the shared-memory attribute is per device: set it once for each device used
+    static std::atomic<uint64_t> attr_set{0};
+    int dev = 0;
+    RAGRT_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
         RAGRT_CUDA_TRY(cudaFuncSetAttribute(enc_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             EncCfg<BN>::kSmem));
-        attr = true;
+        attr_set.fetch_or(bit);
     }
     const int units = (N / BN) * (int)ceil_div(M, kEM) * p.ksplit;
     return enc_launch(enc_gemm<BN>, dim3((unsigned)std::min(units, num_sms())), dim3(kEThreads), EncCfg<BN>::kSmem,
