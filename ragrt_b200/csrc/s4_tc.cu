@@ -82,8 +82,8 @@ struct Cursor {
 // (no codes, residuals or LUT) and the epilogue does not normalise.
 template <bool kRaw>
 __global__ void __launch_bounds__(kTcThreads, 1)
-s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4Docs D, float* __restrict__ out,
-      int* __restrict__ err) {
+s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int cpc, S4Docs D,
+      float* __restrict__ out, int* __restrict__ err) {
     extern __shared__ uint8_t s4_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)s4_raw + 1023) & ~(uintptr_t)1023);
     uint2* lut = reinterpret_cast<uint2*>(sm + kSmLut);
@@ -102,7 +102,7 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.y;
-    const int64_t cbase = (int64_t)blockIdx.x * kTcCandPerCta;
+    const int64_t cbase = (int64_t)blockIdx.x * cpc;     // this CTA: candidates cbase .. cbase + cpc - 1
 
     // ---- stage the codec tables and the candidates' metadata; trivial outputs
     if constexpr (!kRaw) {
@@ -111,9 +111,9 @@ s4_tc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, S4D
         if (tid < 4) tab_bw[tid] = D.bw[tid];
     }
     for (int ci = tid; ci < kTcCandPerCta; ci += kTcThreads) {
-        int L = -1;
+        int L = -1;                                       // slots past cpc stay empty
         int64_t ts = 0;
-        if (cbase + ci < n) {
+        if (ci < cpc && cbase + ci < n) {
             const int64_t slot = (int64_t)b * n + cbase + ci;
             const int32_t pid = pids[slot];
             if (pid < 0 || pid >= D.N) {
@@ -426,11 +426,19 @@ int s4_tc_launch(const __half* Q, const int32_t* pids, int B, int n, const S4Doc
     static_assert(kSmBytes + 1024 <= kSmDynamic, "shared memory map exceeds the allocation");
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s4_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmDynamic));
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s4_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmDynamic));
-    dim3 grid((unsigned)ceil_div(n, kTcCandPerCta), (unsigned)B);
+    // candidates per CTA: 256, or 128 when that fills the last wave of CTAs (one per SM)
+    // clearly better (small per-shard candidate counts)
+    const int sms = num_sms();
+    auto waste = [&](int cpc) {
+        const int64_t ctas = ceil_div((int64_t)n, (int64_t)cpc) * B;
+        return (double)(ceil_div(ctas, (int64_t)sms) * sms) / (double)ctas - 1.0;
+    };
+    const int cpc = waste(kTcCandPerCta / 2) < waste(kTcCandPerCta) - 0.03 ? kTcCandPerCta / 2 : kTcCandPerCta;
+    dim3 grid((unsigned)ceil_div(n, cpc), (unsigned)B);
     if (D.emb)
-        s4_tc<true><<<grid, kTcThreads, kSmDynamic, stream>>>(Q, pids, n, D, out, d_err);
+        s4_tc<true><<<grid, kTcThreads, kSmDynamic, stream>>>(Q, pids, n, cpc, D, out, d_err);
     else
-        s4_tc<false><<<grid, kTcThreads, kSmDynamic, stream>>>(Q, pids, n, D, out, d_err);
+        s4_tc<false><<<grid, kTcThreads, kSmDynamic, stream>>>(Q, pids, n, cpc, D, out, d_err);
     RAGRT_LAUNCH_CHECK();
     return RAGRT_OK;
 }
