@@ -241,6 +241,17 @@ uint64_t ragrt_launch_count(void);
  */
 int ragrt_selftest_wait_timeout(uint32_t polls, void* stream);
 
+/*
+ * Merge of the per-shard top-k lists of a doc-sharded search (one process per GPU, corpus split
+ * by pid range): d_gathered [world][2][B][k] f32 holds, rank-major as an all-gather leaves
+ * them, every rank's scores and global pids (as f32, exact below 2^24; -1 = padding).  Writes
+ * per query the top k_top by (score desc, pid asc), padding after every real pid of equal score:
+ * d_out_ids [B, k_top] int64 (-1 padding), d_out_scores [B, k_top] f32.  No reference
+ * counterpart (the reference searches one GPU).
+ */
+int ragrt_merge_topk(const float* d_gathered, int32_t world, int32_t B, int32_t k, int32_t k_top,
+                     int64_t* d_out_ids, float* d_out_scores, void* stream);
+
 /* ------------------------------------------------------------------------------------ *
  * Stage 0a: the ColBERT query encoder (BERT-base over [B, 32] query tokens, then ColBERT's
  * linear 768 -> 128 and L2 normalisation).  Replaces the reference's flat forward

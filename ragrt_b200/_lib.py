@@ -53,6 +53,7 @@ _SIGS = {
     "ragrt_launch_count": (C.c_uint64, []),
     "ragrt_device_error": (I32, [I32]),
     "ragrt_selftest_wait_timeout": (I32, [C.c_uint32, P]),
+    "ragrt_merge_topk": (I32, [P, I32, I32, I32, I32, P, P, P]),
     "ragrt_enc_gemm": (I32, [P, P, P, P, P, I32, I32, I32, I32, P, I64, P]),
     "ragrt_enc_gemm_residual_ln": (I32, [P, P, P, P, P, P, C.c_float, P, P, I32, I32, I32, P, I64, P]),
     "ragrt_enc_layernorm": (I32, [P, P, P, C.c_float, P, I32, I32, P]),

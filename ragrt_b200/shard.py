@@ -45,6 +45,15 @@ def merge_topk(ids, scores, world, k_top, pid_base, group=None):
     pack = torch.stack([scores.to(torch.float32), gpid.to(torch.float32)], 0)   # pids < 2^24: exact in fp32
     out = torch.empty(world * 2, *pack.shape[1:], dtype=pack.dtype, device=pack.device)
     dist.all_gather_into_tensor(out, pack, group=group)          # rank-major concatenation
+    if out.is_cuda:                                              # one kernel: ragrt_merge_topk
+        from . import _lib
+        from .weft import _ptr, _stream
+        B, k = ids.shape
+        o_ids = torch.empty(B, k_top, dtype=torch.int64, device=out.device)
+        o_sc = torch.empty(B, k_top, dtype=torch.float32, device=out.device)
+        _lib.check(_lib.lib().ragrt_merge_topk(_ptr(out), world, B, k, k_top, _ptr(o_ids), _ptr(o_sc), _stream()))
+        return o_ids, o_sc
+    # gloo ranks on the CPU (the tests of this exchange): the same order with torch sorts
     out = out.view(world, *pack.shape)
     B = ids.shape[0]
     sc = out[:, 0].permute(1, 0, 2).reshape(B, -1)

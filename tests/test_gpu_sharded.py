@@ -157,3 +157,27 @@ def test_sharded_search_single_rank_equals_search(zipf_corpus):
         dist.destroy_process_group()
     rids, rsc = wix.search(Qc, nc=32, K=400, k_top=10)
     assert torch.equal(ids, rids.to(torch.int64)) and torch.equal(sc, rsc)
+
+
+@pytest.mark.parametrize("world,k,k_top", [(8, 10, 10), (3, 7, 12), (1, 10, 5)])
+def test_merge_kernel_orders_like_the_rule(world, k, k_top):
+    """ragrt_merge_topk: (score desc, pid asc), padding (-1) after real pids of equal score --
+    ties, -inf scores and padding included."""
+    from ragrt_b200 import _lib
+    from ragrt_b200.weft import _ptr, _stream
+    g = np.random.default_rng(world * 100 + k)
+    B = 16
+    sc = g.choice(np.array([0.5, 0.25, 1.0, -np.inf, 2.0], np.float32), size=(world, B, k))
+    pid = g.integers(0, 5000, size=(world, B, k)).astype(np.float32)
+    pad = g.random((world, B, k)) < 0.2
+    pid[pad], sc[pad] = -1.0, -np.inf
+    gathered = torch.from_numpy(np.stack([sc, pid], 1).astype(np.float32)).cuda()     # [world, 2, B, k]
+    ids = torch.empty(B, k_top, dtype=torch.int64, device="cuda")
+    out = torch.empty(B, k_top, dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().ragrt_merge_topk(_ptr(gathered), world, B, k, k_top, _ptr(ids), _ptr(out), _stream()))
+    ids, out = ids.cpu().numpy(), out.cpu().numpy()
+    for b in range(B):
+        items = [(float(sc[r, b, j]), int(pid[r, b, j])) for r in range(world) for j in range(k)]
+        items.sort(key=lambda t: (-t[0], t[1] if t[1] >= 0 else 1 << 40))
+        assert ids[b].tolist() == [p for _, p in items[:k_top]]
+        assert np.array_equal(out[b], np.array([s for s, _ in items[:k_top]], np.float32))
