@@ -314,9 +314,12 @@ size_t s3_workspace_bytes(const ragrt_index* ix, int nq_sub) {
 }
 
 int s3_max_sub_batch(const ragrt_index* ix, int B) {
-    // keep the candidate pool under ~2 GiB
+    // The candidate pool holds 8 B per passage per query.  Up to 8 GiB of it lets a whole
+    // batch run as one pass (256 queries over 2 M passages: 4 GB), which avoids a second
+    // pass's tail and gives the selection one CTA per query of the whole batch; larger
+    // batches or corpora run in sub-batches.
     int64_t per_q = (int64_t)ix->d.num_passages * 8;
-    int64_t sub = std::max<int64_t>(1, ((int64_t)2 << 30) / per_q);
+    int64_t sub = std::max<int64_t>(1, ((int64_t)8 << 30) / per_q);
     return (int)std::min<int64_t>(sub, B);
 }
 
