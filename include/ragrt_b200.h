@@ -213,8 +213,10 @@ int ragrt_weft_search_profiled(ragrt_index* index, const void* d_Q, const int32_
  * ragrt_fused_kernel.cu:33-47, :884-899): out[0] queries, out[1] postings scanned
  * (sum over kept (token, probe) pairs of list length), out[2] distinct postings read
  * (each probed list once per query), out[3] passages touched, out[4] kept probes,
- * out[5] candidates reranked.  Synchronises the device.
+ * out[5] candidates reranked.  Synchronises the device.  out[2] needs one extra kernel per
+ * Stage-3 pass and is counted only after ragrt_index_count_distinct(index, 1) (off by default).
  */
+int ragrt_index_count_distinct(ragrt_index* index, int32_t enable);
 #define RAGRT_NUM_STATS 6
 int ragrt_index_stats(ragrt_index* index, uint64_t* out, int32_t reset);
 

@@ -48,6 +48,7 @@ _SIGS = {
     "ragrt_weft_search": (I32, [P, P, P, I32, I32, I32, P, I32, I32, I32, P, P, P]),
     "ragrt_weft_search_profiled": (I32, [P, P, P, I32, I32, I32, P, I32, I32, I32, P, P, P, P]),
     "ragrt_index_stats": (I32, [P, C.POINTER(C.c_uint64), I32]),
+    "ragrt_index_count_distinct": (I32, [P, I32]),
     "ragrt_last_error": (C.c_char_p, []),
     "ragrt_version": (C.c_char_p, []),
     "ragrt_launch_count": (C.c_uint64, []),

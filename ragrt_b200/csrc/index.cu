@@ -299,6 +299,12 @@ extern "C" int ragrt_index_destroy(ragrt_index* ix) {
     return RAGRT_OK;
 }
 
+extern "C" int ragrt_index_count_distinct(ragrt_index* ix, int32_t enable) {
+    RAGRT_REQUIRE(ix, "null index");
+    ix->count_distinct = enable ? 1 : 0;
+    return RAGRT_OK;
+}
+
 extern "C" int ragrt_index_stats(ragrt_index* ix, uint64_t* out, int32_t reset) {
     RAGRT_REQUIRE(ix, "null index");
     if (out) {

@@ -25,6 +25,7 @@ struct ragrt_index {
 
     ragrt_workspace ws;
     unsigned long long* stats = nullptr;   // [RAGRT_NUM_STATS]
+    int count_distinct = 0;                // count out[2] (one extra kernel per Stage-3 pass)
 };
 
 namespace ragrt {

@@ -379,8 +379,10 @@ int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_s
         const int grid = (int)std::min<int64_t>(jobs, (int64_t)per_sm * num_sms());
         s3_accumulate<<<grid, kS3Threads, smem, stream>>>(p);
         RAGRT_LAUNCH_CHECK();
-        s3_query_lists<<<nq, 256, 0, stream>>>(p, counts + sub);
-        RAGRT_LAUNCH_CHECK();
+        if (ix->count_distinct) {             // statistics only: not needed for the result
+            s3_query_lists<<<nq, 256, 0, stream>>>(p, counts + sub);
+            RAGRT_LAUNCH_CHECK();
+        }
         int rc = s3_select_launch(pool, ix->d.num_passages, counts, q0, nq, K, cand_pids, cand_sums, num_touched,
                                   ix->stats, stream);
         if (rc) return rc;

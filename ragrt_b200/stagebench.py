@@ -134,10 +134,13 @@ def main():
         print(f"corpus ready in {time.time() - t0:.1f} s", file=sys.stderr)
         if "s3" in stages:
             topc, sc, _, _ = centroid_topk(Q, C, a.nc)
-            wix.stats(reset=True)
             ms = timed(lambda: wix.candidates(topc, sc, a.K), a.steps, a.warmup)
+            wix.count_distinct(True)          # work counts from one more, untimed pass
+            wix.stats(reset=True)
+            wix.candidates(topc, sc, a.K)
             st = wix.stats()
-            n = a.steps + a.warmup
+            wix.count_distinct(False)
+            n = 1
             b = (3.0 * st["distinct_postings"] + 8.0 * st["touched"]) / n
             out.append({"stage": "s3", "ms": ms, "gbs": b / ms / 1e6, "postings_per_query": st["postings"] / n / a.batch,
                         "distinct_postings_per_query": st["distinct_postings"] / n / a.batch,

@@ -296,7 +296,14 @@ class WeftIndex:
                                                          _stream()))
         return pc, tc
 
+    def count_distinct(self, enable=True):
+        """Count distinct postings per query in stats() (one extra kernel per Stage-3 pass; off
+        by default)."""
+        _lib.check(_lib.lib().ragrt_index_count_distinct(self.handle, int(bool(enable))))
+
     def stats(self, reset=False):
+        """Counters since the last reset: queries, postings (scanned), distinct_postings (only
+        while count_distinct is on), touched, probes, candidates."""
         buf = (C.c_uint64 * _lib.NUM_STATS)()
         _lib.check(_lib.lib().ragrt_index_stats(self.handle, buf, int(bool(reset))))
         return dict(zip(_lib.STAT_NAMES, list(buf)))
