@@ -8,7 +8,7 @@
 //
 //   enc_gemm       D[M, N] = A[M, K] . W[N, K]^T on the tensor cores (tcgen05.mma kind::f16,
 //                  fp32 accumulators in tensor memory), A and W tiles brought in by TMA
-//                  (128-byte swizzle, K-major, no multicast).  Fused epilogues: + bias,
+//                  (128-byte swizzle, K-major, each CTA loads its own tiles).  Fused epilogues: + bias,
 //                  gelu (erf or tanh form), + residual, or the final fp16 rounding + L2
 //                  normalisation of a 128-wide row.  Warp 0 issues the TMA loads, warp 1 the
 //                  MMAs, warps 2-9 drain the accumulator (two per 32-row quadrant, each
