@@ -31,3 +31,26 @@ def test_argument_errors_need_no_gpu():
     assert rc == -1 and b"null" in L.ragrt_last_error()
     rc = L.ragrt_index_create(None, None, None)
     assert rc == -1
+
+
+def test_new_entry_points_reject_bad_arguments_without_a_gpu():
+    """The encoder, merge and statistics entry points validate their arguments before any
+    CUDA call (fake non-null pointers: nothing is dereferenced on these paths)."""
+    L = _lib.lib()
+    p = 0x1000                                          # 16-byte aligned, never touched
+    # N not a multiple of 128
+    assert L.ragrt_enc_gemm(p, p, None, None, p, 64, 100, 768, 0, None, 0, None) == -1
+    assert b"multiple of 128" in L.ragrt_last_error()
+    # the normalising epilogue is for N = 128
+    assert L.ragrt_enc_gemm(p, p, None, None, p, 64, 256, 768, 4, None, 0, None) == -1
+    # the residual epilogue needs a residual
+    assert L.ragrt_enc_gemm(p, p, p, None, p, 64, 256, 768, 3, None, 0, None) == -1
+    # attention is built for 32 tokens and 64-wide heads
+    assert L.ragrt_enc_attention(p, p, p, 2, 16, 12, 768, None) == -1
+    assert L.ragrt_enc_attention(p, p, p, 2, 32, 12, 700, None) == -1
+    assert L.ragrt_enc_layernorm(p, p, p, 1e-12, p, 8, 512, None) == -1
+    assert L.ragrt_enc_gemm_residual_ln(p, p, p, p, p, p, 1e-12, p, p, 64, 512, 768, None, 0, None) == -1
+    # merge: k_top beyond world * k, and null outputs
+    assert L.ragrt_merge_topk(p, 2, 4, 10, 21, p, p, None) == -1
+    assert L.ragrt_merge_topk(p, 2, 4, 10, 10, None, p, None) == -1
+    assert L.ragrt_index_count_distinct(None, 1) == -1
