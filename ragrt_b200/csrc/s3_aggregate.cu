@@ -33,7 +33,8 @@ namespace ragrt {
 
 constexpr int kS3Warps = 8;
 constexpr int kS3Threads = kS3Warps * 32;
-constexpr int kS3RangesPerJob = 8;   // consecutive pid ranges of one query per work item (one probe table)
+constexpr int kS3RangesPerJob = 8;   // consecutive pid ranges of one query per work item (one probe table),
+                                     // fewer when the items would not give each CTA several
 constexpr int kS3Batch = 8;       // 32-posting chunks whose pid loads a warp keeps in flight together
 
 struct S3Params {
@@ -53,6 +54,7 @@ struct S3Params {
     const int32_t* ntok;
     const uint32_t* masks;
     int q0, nq;                  // queries [q0, q0 + nq) of the batch
+    int rpj;                     // pid ranges per work item
     // output
     uint64_t* pool;              // [nq][pool_cap]
     int64_t pool_cap;
@@ -86,7 +88,7 @@ s3_accumulate(S3Params p) {
     for (int i = tid; i < kS3Warps * (W >> 5); i += kS3Threads) seen[i] = 0u;
     unsigned long long st_post = 0, st_probes = 0;
     int cached_q = -1;
-    const unsigned nrb = ((unsigned)p.R + kS3RangesPerJob - 1) / kS3RangesPerJob;
+    const unsigned nrb = ((unsigned)p.R + p.rpj - 1) / p.rpj;
     const unsigned total_jobs = (unsigned)p.nq * nrb;
     __syncthreads();
 
@@ -96,7 +98,7 @@ s3_accumulate(S3Params p) {
         const unsigned job = s_unit;
         if (job >= total_jobs) break;
         const int qi = (int)(job / nrb);
-        const int r0 = (int)(job % nrb) * kS3RangesPerJob, r1 = min(p.R, r0 + kS3RangesPerJob);
+        const int r0 = (int)(job % nrb) * p.rpj, r1 = min(p.R, r0 + p.rpj);
       for (int r = r0; r < r1; ++r) {
         const int q = p.q0 + qi;
         const uint32_t mask = p.masks ? p.masks[q] : 0u;
@@ -375,8 +377,15 @@ int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_s
         p.work = work;
         p.stats = ix->stats;
         if (masks && !ix->d.doc_predicates) p.masks = nullptr;   // no predicates bound: no filter
-        const int64_t jobs = (int64_t)nq * ((ix->num_ranges + kS3RangesPerJob - 1) / kS3RangesPerJob);
-        const int grid = (int)std::min<int64_t>(jobs, (int64_t)per_sm * num_sms());
+        // 8 ranges per work item (the probe table is built once per item), halved while the
+        // items would give the persistent CTAs fewer than 8 each (small shards): the last
+        // round of a few large items leaves CTAs idle
+        const int64_t ctas = (int64_t)per_sm * num_sms();
+        int rpj = kS3RangesPerJob;
+        while (rpj > 1 && (int64_t)nq * ((ix->num_ranges + rpj - 1) / rpj) < 8 * ctas) rpj >>= 1;
+        p.rpj = rpj;
+        const int64_t jobs = (int64_t)nq * ((ix->num_ranges + rpj - 1) / rpj);
+        const int grid = (int)std::min<int64_t>(jobs, ctas);
         s3_accumulate<<<grid, kS3Threads, smem, stream>>>(p);
         RAGRT_LAUNCH_CHECK();
         if (ix->count_distinct) {             // statistics only: not needed for the result
