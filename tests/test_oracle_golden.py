@@ -216,3 +216,24 @@ def test_plain_ivf_and_packing_golden():
     for bad in ([L.MAX_PID + 1], [-1]):
         with pytest.raises(OverflowError):
             L.pack_pids_24(np.array(bad))
+
+
+def test_torch_index_builder_matches_reference_golden():
+    """ragrt_b200.index_build (the corpus-scale builder, torch on CPU or GPU) produces the
+    reference builder's arrays on the golden fixture: row pointers, chunk ids, lengths, the
+    128-list block sums and the 24-bit packed pids, for the default and a tiny list cap."""
+    import torch
+    from ragrt_b200 import index_build
+    g = _load("plain_ivf")
+    codes = torch.from_numpy(np.asarray(g["codes"], np.int32))
+    dl = torch.from_numpy(np.asarray(g["doclens"], np.int32))
+    for ml in (65535, 5):
+        ix = index_build.plain_ivf_index(codes, dl, int(g["num_centroids"]), max_len=ml)
+        assert np.array_equal(ix["csr_row_ptrs"].numpy(), g[f"row_ptrs_{ml}"]), ml
+        assert np.array_equal(ix["csr_col_eids"].numpy().astype(np.int64), g[f"col_eids_{ml}"].astype(np.int64)), ml
+        lens = ix["csr_lengths"].view(torch.int16).numpy().view(np.uint16).astype(np.int64)
+        assert np.array_equal(lens, g[f"lengths_{ml}"].astype(np.int64)), ml
+        assert np.array_equal(ix["csr_block_sums"].numpy(), g[f"block_sums_{ml}"]), ml
+        assert np.array_equal(ix["csr_packed_24"].numpy(), g[f"packed_{ml}"]), ml
+        assert ix["num_postings"] == len(g[f"pids_sorted_{ml}"])
+        assert ix["E"] == max(4, int(g[f"E_needed_{ml}"]))
