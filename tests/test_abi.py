@@ -1,7 +1,5 @@
 """The C-ABI library loads on a CPU-only host and exports every entry point that
 include/ragrt_b200.h declares (no compute calls: those need a GPU)."""
-import ctypes as C
-import os
 
 from ragrt_b200 import _lib
 

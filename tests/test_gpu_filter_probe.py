@@ -4,7 +4,6 @@ index arrays, and the probe selections against the same rules applied to the CPU
 Stage-2 scores (bit-exact: both rank by the exact fp16 score, ties to the lower centroid)."""
 import numpy as np
 import pytest
-import torch
 
 from oracle import oracle as O
 from ragrt_b200.compat import weft_prep as wp

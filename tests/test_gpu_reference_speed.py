@@ -16,7 +16,6 @@ the per-query times (run with -s to see it).
 import ctypes as C
 import json
 
-import numpy as np
 import pytest
 import torch
 
