@@ -33,16 +33,21 @@ def _p(t):
     return C.c_void_p(t.data_ptr())
 
 
-def _ms(fn, reps=3):
+def _ms(fn, reps=3, rounds=3):
+    """Mean time of `reps` calls after a warm-up, the best of `rounds` rounds (the same for the
+    reference and for ours), so that one disturbance on a shared GPU does not decide the test."""
     fn()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        fn()
-    e1.record()
-    torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / reps
+    best = float("inf")
+    for _ in range(rounds):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) / reps)
+    return best
 
 
 def _ref_native_prep(q, C16, nc):
