@@ -4,8 +4,8 @@
 //   score(pid) = sum_r max_t (q_r . d_t) * rsqrt(|d_t|^2 + 1e-12)
 // with d_t = fp16(centroid[code_t] + bucket_weight[bucket of dim]) per dim.
 //
-// Warp-specialised pipeline, one CTA per SM, 256 candidates per CTA in 4 streams (stream q
-// = candidates q, q+4, ...; chunks of 32 tokens, one candidate per chunk).  Tile k of the
+// Warp-specialised pipeline, one CTA per SM, cpc = 256 (or 128) candidates per CTA in 4 streams
+// (stream q = candidates q, q+4, ...; chunks of 32 tokens, one candidate per chunk).  Tile k of the
 // CTA holds chunk k of every stream, stream q in tensor-memory lane quadrant q:
 //   * 8 decoder warps (warp w: quadrant w % 4, tiles k = w / 4 mod 2).  For its next chunk a
 //     decoder issues coalesced 16-byte cp.async copies (a half-warp per 256-byte centroid
