@@ -68,3 +68,30 @@ def weft_index(d, E):
     g = to_cuda(d)
     return WeftIndex(*[g[k] for k in BIND_KEYS], num_passages=g["doc_lens"].shape[0],
                      num_centroids=g["centroids"].shape[0], E=E)
+
+
+MAX_PASSAGES = 1 << 24                    # 24-bit packed pids (ragrt_index_lib.py:23-24)
+
+
+@functools.lru_cache(maxsize=1)
+def max_pid_corpus(num_docs=2000, nq=4):
+    """The largest corpus the 24-bit posting format holds: 2^24 passages, of which only the
+    first and the last num_docs/2 have tokens (the documents of small_corpus), so pids reach
+    2^24 - 1 while the arrays stay small.  Returns (d, Q, E, pid_map): pid_map[i] is the pid of
+    small_corpus document i in this corpus."""
+    d0, Q, _, _ = small_corpus(num_docs=num_docs, nq=nq)
+    N, half = MAX_PASSAGES, num_docs // 2
+    pid_map = torch.cat([torch.arange(half), torch.arange(N - (num_docs - half), N)])
+    doclens = torch.zeros(N, dtype=torch.int32)
+    doclens[pid_map] = d0["doc_lens"]
+    offsets = torch.zeros(N + 1, dtype=torch.int64)
+    offsets[1:] = torch.cumsum(doclens.long(), 0)
+    preds = torch.zeros(N, dtype=torch.int64)
+    preds[pid_map] = d0["doc_predicates"].to(torch.int64)
+    ix = index_build.plain_ivf_index(d0["codes"], doclens, d0["centroids"].shape[0])
+    d = dict(d0)
+    d.update({"csr_row_ptrs": ix["csr_row_ptrs"], "csr_col_eids": ix["csr_col_eids"],
+              "csr_block_sums": ix["csr_block_sums"], "csr_lengths": ix["csr_lengths"],
+              "csr_packed_24": ix["csr_packed_24"], "doc_offsets": offsets, "doc_lens": doclens,
+              "doc_predicates": preds.to(torch.uint32)})
+    return d, Q, ix["E"], pid_map
