@@ -310,13 +310,17 @@ class CorrIndex3D:
         return out
 
     def search_batch(self, Q_fp16, k_cent, k_candidates, k_top, query_mask=0, ntok=None):
-        """New batched entry: Stage 2 included.  Q_fp16 [B, 32, 128] -> (ids [B, k_top], scores)."""
+        """New batched entry: Stage 2 included.  Q_fp16 [B, 32, 128] -> (ids [B, k_top], scores).
+        query_mask: one uint32 for the batch or a per-query tensor [B]; ntok: per-query token
+        counts [B] (list or tensor).  Host-side masks / ntok are moved to Q's device."""
         if self._ix is None:
             raise RuntimeError("Index must be bound before search!")
         B = Q_fp16.shape[0]
+        if ntok is not None:
+            ntok = torch.as_tensor(ntok, dtype=torch.int32).to(Q_fp16.device)
         masks = None
         if torch.is_tensor(query_mask):
-            masks = query_mask.to(torch.int64).bitwise_and(0xFFFFFFFF).to(torch.int32)
+            masks = query_mask.to(torch.int64).bitwise_and(0xFFFFFFFF).to(torch.int32).to(Q_fp16.device)
         elif query_mask:
             masks = torch.full((B,), int(query_mask) & 0xFFFFFFFF, dtype=torch.int64,
                                device=Q_fp16.device).to(torch.int32)

@@ -3,11 +3,11 @@ Doc-range sharding of the `weft` path over several GPUs (one process per GPU).
 
 Each rank holds the passages [lo, hi) of the corpus (contiguous pid range) with its own
 plain-IVF index over local pids, runs Stages 2-4 locally and produces its top-k as
-(score, local pid).  `merge_topk` moves every rank's list with one all-gather and merges by
-(score desc, global pid asc), the tie rule this build uses for every final selection (the
-reference's torch::topk at src/optix_corr_torch_3d.cpp:603-606 leaves ties unspecified).  The
-result equals running each shard alone and merging; because the
-candidate budget applies per shard it is not the 1-GPU result over the union of shards.
+(score, local pid).  `merge_topk` moves every rank's list with one all-gather (`gather_topk`)
+and merges them on the GPU by (score desc, global pid asc), the tie rule this build uses for
+every final selection (the reference's torch::topk at src/optix_corr_torch_3d.cpp:603-606
+leaves ties unspecified).  The result equals running each shard alone and merging; because
+the candidate budget applies per shard it is not the 1-GPU result over the union of shards.
 
 Stage 2 (query tokens x centroids) does not depend on the shard, so `sharded_search` does not
 repeat it on every rank: rank r scores its slice of the query batch and `gather_probes` gives
@@ -36,33 +36,32 @@ def slice_docs(doc_offsets, doclens, codes, residuals, preds, lo, hi):
     }
 
 
-def merge_topk(ids, scores, world, k_top, pid_base, group=None):
-    """ids int32 [B, k] (local pids, -1 padding), scores f32 [B, k] (-inf padding) on this
-    rank -> (global pids int64 [B, k_top], scores f32 [B, k_top]) merged over all ranks.
-    Uses one all_gather_into_tensor (NCCL on GPUs, gloo on CPU)."""
+def gather_topk(ids, scores, world, pid_base, group=None):
+    """ids int32 [B, k] (local pids, -1 padding), scores f32 [B, k] (-inf padding) on this rank
+    -> every rank's list, rank-major, as f32 [world * 2, B, k] (scores, then global pids; pids
+    < 2^24 are exact in fp32, padding stays -1), with one all_gather_into_tensor."""
     import torch.distributed as dist
     gpid = torch.where(ids >= 0, ids.to(torch.int64) + pid_base, torch.full_like(ids, -1, dtype=torch.int64))
-    pack = torch.stack([scores.to(torch.float32), gpid.to(torch.float32)], 0)   # pids < 2^24: exact in fp32
+    pack = torch.stack([scores.to(torch.float32), gpid.to(torch.float32)], 0)
     out = torch.empty(world * 2, *pack.shape[1:], dtype=pack.dtype, device=pack.device)
-    dist.all_gather_into_tensor(out, pack, group=group)          # rank-major concatenation
-    if out.is_cuda:                                              # one kernel: ragrt_merge_topk
-        from . import _lib
-        from .weft import _ptr, _stream
-        B, k = ids.shape
-        o_ids = torch.empty(B, k_top, dtype=torch.int64, device=out.device)
-        o_sc = torch.empty(B, k_top, dtype=torch.float32, device=out.device)
-        _lib.check(_lib.lib().ragrt_merge_topk(_ptr(out), world, B, k, k_top, _ptr(o_ids), _ptr(o_sc), _stream()))
-        return o_ids, o_sc
-    # gloo ranks on the CPU (the tests of this exchange): the same order with torch sorts
-    out = out.view(world, *pack.shape)
-    B = ids.shape[0]
-    sc = out[:, 0].permute(1, 0, 2).reshape(B, -1)
-    pid = out[:, 1].permute(1, 0, 2).reshape(B, -1).to(torch.int64)
-    key = torch.where(pid >= 0, pid, torch.full_like(pid, 1 << 40))
-    order = torch.argsort(key, dim=1, stable=True)                       # pid asc ...
-    sc, pid = torch.gather(sc, 1, order), torch.gather(pid, 1, order)
-    order = torch.argsort(sc, dim=1, descending=True, stable=True)       # ... then score desc
-    return torch.gather(pid, 1, order)[:, :k_top], torch.gather(sc, 1, order)[:, :k_top]
+    dist.all_gather_into_tensor(out, pack, group=group)
+    return out
+
+
+def merge_topk(ids, scores, world, k_top, pid_base, group=None):
+    """ids int32 [B, k] (local pids, -1 padding), scores f32 [B, k] (-inf padding) on this
+    rank's GPU -> (global pids int64 [B, k_top], scores f32 [B, k_top]) merged over all ranks
+    by (score desc, pid asc): gather_topk, then one ragrt_merge_topk kernel."""
+    if not (ids.is_cuda and scores.is_cuda):
+        raise RuntimeError("ragrt_b200 runs on CUDA tensors only (there is no CPU path)")
+    from . import _lib
+    from .weft import _ptr, _stream
+    out = gather_topk(ids, scores, world, pid_base, group=group)
+    B, k = ids.shape
+    o_ids = torch.empty(B, k_top, dtype=torch.int64, device=out.device)
+    o_sc = torch.empty(B, k_top, dtype=torch.float32, device=out.device)
+    _lib.check(_lib.lib().ragrt_merge_topk(_ptr(out), world, B, k, k_top, _ptr(o_ids), _ptr(o_sc), _stream()))
+    return o_ids, o_sc
 
 
 def query_slice(B, world, rank):

@@ -27,9 +27,21 @@ def _ptr(t):
 
 
 def _need_cuda(*ts):
+    """Every tensor argument of a call (None for an absent optional one) must live on the
+    current CUDA device: the kernels dereference each pointer on that device, on torch's
+    current stream."""
+    dev = None
     for t in ts:
-        if t is not None and not t.is_cuda:
+        if t is None:
+            continue
+        if not t.is_cuda:
             raise RuntimeError("ragrt_b200 runs on CUDA tensors only (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors of one call are on {dev} and {t.device}: all must be on one device")
+    if dev is not None and dev.index != torch.cuda.current_device():
+        raise RuntimeError(f"tensors are on {dev} but the current device is cuda:{torch.cuda.current_device()}")
 
 
 def _c(t, dtype):
@@ -40,7 +52,7 @@ def centroid_topk(Q, C_, nc, impute=True, ntok=None, full=False):
     """Stage 2 for a batch.  Q [B, rows, 128] (rows <= 32) fp16 CUDA, C [NC, 128] fp16.
     Returns (topc int32 [B, rows, ncol], scores f32 [B, rows, ncol], m f32 [B, rows],
     full16 fp16 [B, rows, NC] or None); ncol = min(nc, min(nc + impute, NC))."""
-    _need_cuda(Q, C_)
+    _need_cuda(Q, C_, ntok)
     Q = _c(Q, torch.float16)
     C_ = _c(C_, torch.float16)
     if Q.dim() == 2:
@@ -85,7 +97,8 @@ def tile_maxsim_exact(Q, pids, doc_offsets, doc_lens, doc_emb):
 def tile_maxsim(Q, pids, doc_offsets, doc_lens, codes, residuals, centroids, bucket_weights,
                 reversed_bit_map, decomp_table, mode=1):
     """Stage 4.  Q [B, 32, 128] (or [32, 128]) fp16, pids [B, n] (or [n]) int32 -> f32 scores."""
-    _need_cuda(Q, pids, doc_offsets, doc_lens, codes, residuals, centroids)
+    _need_cuda(Q, pids, doc_offsets, doc_lens, codes, residuals, centroids, bucket_weights, reversed_bit_map,
+               decomp_table)
     squeeze = Q.dim() == 2
     Q = _c(Q, torch.float16)
     if squeeze:
@@ -112,7 +125,7 @@ def tile_maxsim(Q, pids, doc_offsets, doc_lens, codes, residuals, centroids, buc
 
 def final_topk(pids, scores, k, preds=None, masks=None, num_preds=None):
     """Failing / padding candidates -> -inf, then top-k by (score desc, pid asc)."""
-    _need_cuda(pids, scores)
+    _need_cuda(pids, scores, preds, masks)
     pids = _c(pids, torch.int32)
     scores = _c(scores, torch.float32)
     if pids.dim() == 1:
@@ -138,7 +151,8 @@ class WeftIndex:
                  doc_offsets, doc_lens, codes, residuals, centroids, bucket_weights, reversed_bit_map,
                  decomp_table, doc_predicates=None, num_passages=None, num_centroids=None, E=None):
         _need_cuda(csr_row_ptrs, csr_col_eids, csr_block_sums, csr_lengths, csr_packed_24, doc_offsets,
-                   doc_lens, codes, residuals, centroids)
+                   doc_lens, codes, residuals, centroids, bucket_weights, reversed_bit_map, decomp_table,
+                   doc_predicates)
         if csr_col_eids.element_size() not in (1, 2):
             raise RuntimeError("csr_col_eids must be 8- or 16-bit")
         if csr_lengths.element_size() != 2:
@@ -224,7 +238,7 @@ class WeftIndex:
     def candidates(self, topc, scores, K, ntok=None, masks=None, n_eids=None, full_scores=False):
         """Stages 1-3: topc [B, rows, kc], scores (compact [B, rows, kc] or full [B, rows, NC]).
         Returns (pids int32 [B, K] -1-padded, sums f32 [B, K] -inf-padded, touched int64 [B])."""
-        _need_cuda(topc, scores)
+        _need_cuda(topc, scores, ntok, masks)
         topc = _c(topc, torch.int32)
         scores = _c(scores, torch.float32)
         if topc.dim() == 2:
@@ -250,7 +264,7 @@ class WeftIndex:
 
     def search(self, Q, nc=32, K=4096, k_top=10, ntok=None, masks=None, rerank="tc", n_eids=None, out=None):
         """The fused batched search.  Q [B, 32, 128] fp16 -> (ids int32 [B, k_top], scores f32)."""
-        _need_cuda(Q)
+        _need_cuda(Q, ntok, masks, *(out or ()))
         Q = _c(Q, torch.float16)
         if Q.dim() == 2:
             Q = Q[None]
@@ -270,6 +284,7 @@ class WeftIndex:
     def search_profiled(self, Q, events, nc=32, K=4096, k_top=10, ntok=None, masks=None, rerank="tc",
                         n_eids=None, out=None):
         """search() recording 5 torch.cuda.Event objects at the stage boundaries (no sync)."""
+        _need_cuda(Q, ntok, masks, *(out or ()))
         Q = _c(Q, torch.float16)
         B = Q.shape[0]
         ids, sc = out if out is not None else (torch.empty(B, k_top, dtype=torch.int32, device=Q.device),

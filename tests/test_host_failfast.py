@@ -49,3 +49,45 @@ def test_dropin_rejects_bad_configuration():
         idx.search_single_query_native(None, None, torch.zeros(4, 32, 3), None, None, 8, 10, 5)
     idx.build(torch.zeros(32, 8, 3))
     assert idx.info()["num_entries"] == 8
+
+
+class _Stop(Exception):
+    pass
+
+
+def test_every_tensor_argument_is_device_checked(monkeypatch):
+    """Each entry point hands ALL of its tensor arguments -- optional ones such as ntok, masks,
+    predicates and output buffers included -- to the device check before any pointer reaches
+    the library: a host tensor there would be dereferenced on the device."""
+    seen = []
+
+    def record(*ts):
+        seen.append(ts)
+        raise _Stop
+
+    monkeypatch.setattr(weft, "_need_cuda", record)
+    T = [torch.zeros(1) for _ in range(16)]
+
+    def checked(fn, *args, expect, **kw):
+        seen.clear()
+        with pytest.raises(_Stop):
+            fn(*args, **kw)
+        got = {id(t) for t in seen[0] if t is not None}
+        missing = [i for i, t in enumerate(expect) if id(t) not in got]
+        assert not missing, (fn.__name__, missing)
+
+    checked(weft.centroid_topk, T[0], T[1], 8, ntok=T[2], expect=T[:3])
+    checked(weft.tile_maxsim, *T[:10], expect=T[:10])
+    checked(weft.tile_maxsim_exact, *T[:5], expect=T[:5])
+    checked(weft.final_topk, T[0], T[1], 4, preds=T[2], masks=T[3], expect=T[:4])
+    checked(weft.WeftIndex, *T[:13], doc_predicates=T[13], expect=T[:14])
+    ix = object.__new__(weft.WeftIndex)
+    checked(ix.candidates, T[0], T[1], 10, ntok=T[2], masks=T[3], expect=T[:4])
+    checked(ix.search, T[0], ntok=T[1], masks=T[2], out=(T[3], T[4]), expect=T[:5])
+    checked(ix.search_profiled, T[0], [], ntok=T[1], masks=T[2], out=(T[3], T[4]), expect=T[:5])
+
+
+def test_device_check_refuses_host_tensors_among_cuda_ones():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        weft._need_cuda(None, torch.zeros(1))
+    weft._need_cuda(None, None)                                  # nothing to check

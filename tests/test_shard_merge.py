@@ -1,12 +1,14 @@
 """Doc-range sharding on CPU with world_size-2 `gloo` ranks: every rank slices its shard of a
-small corpus, runs the CPU restatement of the whole path (oracle) on it, and merges the
-per-shard top-k with ragrt_b200.shard.merge_topk (the same function bench.py runs over NCCL).
-The merged list must equal the single-process merge of both shards' results by (score desc,
-global pid asc), on every rank."""
+small corpus, runs the CPU restatement of the whole path (oracle) on it, and exchanges the
+per-shard top-k with ragrt_b200.shard.gather_topk (the all-gather that merge_topk runs over
+NCCL before its merge kernel).  Merged by the rule (score desc, global pid asc), the exchanged
+lists must equal the single-process merge of both shards' results, on every rank.  The merge
+kernel itself is checked against the same rule on the GPU (test_gpu_sharded.py)."""
 import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -51,10 +53,24 @@ def _worker(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         ids, sc, lo = _shard_search(rank, world)
-        g_ids, g_sc = shard.merge_topk(torch.from_numpy(ids), torch.from_numpy(sc), world, K_TOP, lo)
+        out = shard.gather_topk(torch.from_numpy(ids), torch.from_numpy(sc), world, lo)
+        g_ids, g_sc = _merge_rule(out, world, ids.shape[0], K_TOP)
         q.put((rank, g_ids.numpy(), g_sc.numpy()))
     finally:
         dist.destroy_process_group()
+
+
+def _merge_rule(gathered, world, B, k_top):
+    """The merge rule applied to gather_topk's output f32 [world * 2, B, k] with torch sorts:
+    score desc, then pid asc, padding (-1) after every real pid of equal score."""
+    out = gathered.view(world, 2, B, -1)
+    sc = out[:, 0].permute(1, 0, 2).reshape(B, -1)
+    pid = out[:, 1].permute(1, 0, 2).reshape(B, -1).to(torch.int64)
+    key = torch.where(pid >= 0, pid, torch.full_like(pid, 1 << 40))
+    order = torch.argsort(key, dim=1, stable=True)                       # pid asc ...
+    sc, pid = torch.gather(sc, 1, order), torch.gather(pid, 1, order)
+    order = torch.argsort(sc, dim=1, descending=True, stable=True)       # ... then score desc
+    return torch.gather(pid, 1, order)[:, :k_top], torch.gather(sc, 1, order)[:, :k_top]
 
 
 def _expected(world):
@@ -72,6 +88,13 @@ def _expected(world):
         for j, (s, p) in enumerate(items[:K_TOP]):
             out_sc[b, j], out_ids[b, j] = s, p
     return out_ids, out_sc
+
+
+def test_merge_refuses_host_tensors():
+    """No CPU path: merge_topk raises before it enters the collective."""
+    ids = torch.zeros(2, K_TOP, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        shard.merge_topk(ids, torch.zeros(2, K_TOP), WORLD, K_TOP, 0)
 
 
 def test_slice_docs_covers_corpus():
