@@ -21,7 +21,7 @@ the reference; `encode_ids` takes already-tokenized input.
 import torch
 
 from . import _lib
-from .weft import _ptr, _stream
+from .weft import _need_cuda, _ptr, _stream
 
 EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_GELU_TANH, EPI_BIAS_RESIDUAL, EPI_NORM = 0, 1, 2, 3, 4
 
@@ -102,8 +102,7 @@ def _layernorm(x, ln, eps, out):
 def flat_forward(W, ids, mask):
     """ids, mask [B, L] (int64, on the weights' device) -> unit ColBERT query vectors
     [B, L, dim] fp16.  Needs L = 32, hidden size 768 and head size 64 (BERT-base)."""
-    if not ids.is_cuda:
-        raise RuntimeError("ragrt_b200 runs on CUDA tensors only (there is no CPU path)")
+    _need_cuda(ids, mask, W["emb_word"])
     ids = ids.to(torch.int64).contiguous()
     mask = mask.to(torch.int64).contiguous()
     B, L = ids.shape
