@@ -56,13 +56,13 @@ typedef struct {
     const int32_t*  doc_lens;         /* [num_passages]                                       */
     const int32_t*  codes;            /* [num_tokens]                                         */
     const uint8_t*  residuals;        /* [num_tokens, 32], 16-byte aligned                    */
-    int64_t         num_tokens;
+    int64_t         num_tokens;       /* every passage's tokens lie in [0, num_tokens)        */
     const void*     centroids;        /* fp16 [num_centroids, 128], 16-byte aligned           */
     const void*     bucket_weights;   /* fp16 [4]                                             */
     const uint8_t*  reversed_bit_map; /* [256]                                                */
     const uint8_t*  decomp_table;     /* [256, 4]                                             */
     const uint32_t* doc_predicates;   /* [num_passages]; may be NULL (no filters)             */
-    int32_t         num_passages;     /* N  (< 2^24)                                          */
+    int32_t         num_passages;     /* N <= 2^24 (24-bit pids)                              */
     int32_t         num_centroids;    /* NC                                                   */
     int32_t         num_eids;         /* E: chunk ids enumerated per probed centroid          */
 } ragrt_index_desc;

@@ -89,7 +89,19 @@ enum : int {
     kBadEids = 1 << 2,       // a centroid's chunk ids are not 0..k-1
     kBadOffsets = 1 << 3,    // block sums disagree with the lengths
     kBadPids = 1 << 4,       // a pid >= N or pids of a centroid not sorted
+    kBadDocs = 1 << 5,       // a passage's tokens are not inside [0, num_tokens)
 };
+
+// thread per passage: its tokens [doc_offsets[i], doc_offsets[i] + doc_lens[i]) lie inside
+// the bound codes / residuals, so Stage 4 never reads past them
+__global__ void k_check_docs(const int64_t* __restrict__ off, const int32_t* __restrict__ lens, int N,
+                             int64_t num_tokens, int* __restrict__ flags) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= N) return;
+    const int64_t o = off[i];
+    const int32_t L = lens[i];
+    if (o < 0 || L < 0 || o > num_tokens - L) atomicOr(flags, kBadDocs);
+}
 
 __global__ void k_list_offsets(const int64_t* __restrict__ bsums, const uint16_t* __restrict__ lengths,
                                int64_t num_lists, int64_t* __restrict__ off) {
@@ -196,7 +208,7 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
     RAGRT_REQUIRE(d.num_centroids >= 1, "num_centroids must be >= 1");
     RAGRT_REQUIRE(d.num_eids >= 1 && d.num_eids <= (d.eid_bytes == 1 ? 256 : 65536),
                   "E=%d does not fit %d-bit eids", d.num_eids, 8 * d.eid_bytes);
-    RAGRT_REQUIRE(d.num_lists >= 0 && d.num_postings >= 0, "negative sizes");
+    RAGRT_REQUIRE(d.num_lists >= 0 && d.num_postings >= 0 && d.num_tokens >= 0, "negative sizes");
     RAGRT_REQUIRE(((uintptr_t)d.residuals & 15) == 0 && ((uintptr_t)d.centroids & 15) == 0,
                   "residuals and centroids must be 16-byte aligned");
 
@@ -246,6 +258,8 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
         k_check_lists<<<(unsigned)ceil_div(d.num_lists, T), T, 0, stream>>>(ix->list_off, d.csr_lengths, d.num_lists,
                                                                            d.num_postings, flags);
     k_check_rows<<<(unsigned)ceil_div((int64_t)31 * (NC + 1), T), T, 0, stream>>>(d.csr_row_ptrs, NC, flags);
+    k_check_docs<<<(unsigned)ceil_div((int64_t)d.num_passages, T), T, 0, stream>>>(d.doc_offsets, d.doc_lens,
+                                                                                 d.num_passages, d.num_tokens, flags);
     if (d.eid_bytes == 1)
         k_centroids<uint8_t><<<(unsigned)ceil_div(NC, T), T, 0, stream>>>(
             d.csr_row_ptrs, (const uint8_t*)d.csr_col_eids, NC, d.num_lists, ix->list_off, ix->cstart, ix->clists, flags);
@@ -259,11 +273,12 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
     if (h_flags) {
         cudaFree(flags);
         return cleanup(fail(RAGRT_ERR_INDEX,
-                            "not a valid plain-IVF index (flags 0x%x:%s%s%s%s)", h_flags,
+                            "not a valid plain-IVF index (flags 0x%x:%s%s%s%s%s)", h_flags,
                             (h_flags & kBadRow0) ? " row_ptrs row 0 malformed;" : "",
                             (h_flags & kBadRows) ? " subspace rows 1-31 not empty (weft needs a plain-IVF index);" : "",
                             (h_flags & kBadEids) ? " chunk ids of a centroid are not 0..k-1;" : "",
-                            (h_flags & kBadOffsets) ? " block sums disagree with lengths / num_postings;" : ""));
+                            (h_flags & kBadOffsets) ? " block sums disagree with lengths / num_postings;" : "",
+                            (h_flags & kBadDocs) ? " doc_offsets / doc_lens reach outside the num_tokens codes;" : ""));
     }
     k_check_pids<<<(unsigned)ceil_div((int64_t)NC * 32, T), T, 0, stream>>>(d.csr_packed_24, ix->cstart, ix->clists,
                                                                           d.csr_row_ptrs, ix->list_off, NC,

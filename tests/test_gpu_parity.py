@@ -201,6 +201,20 @@ def test_invalid_index_is_rejected():
         mk(bad, E)
 
 
+def test_documents_outside_the_codes_are_rejected():
+    """A passage whose tokens reach past the bound codes / residuals fails at bind time (the
+    search, which would read them on the device, never runs)."""
+    d, Q, E, _ = small_corpus()
+    from ragrt_b200._lib import RagrtError
+    from tests.helpers import weft_index as mk
+    bad = dict(d)
+    lens = d["doc_lens"].clone()
+    lens[-1] += 5                                 # the last passage ends 5 tokens past the codes
+    bad["doc_lens"] = lens
+    with pytest.raises(RagrtError, match="outside the num_tokens codes"):
+        mk(bad, E)
+
+
 @pytest.mark.parametrize("nq,ntok_drop", [(8, 0), (5, 7)])
 def test_stage2_tensor_core_many_tiles(nq, ntok_drop):
     """Stage 2 with several 128-row tiles and centroid slices (the tcgen05 path) is bit-exact."""
