@@ -237,15 +237,45 @@ def host_oracle_index(cents, corp, shard, ix):
     return O.Index(host)
 
 
-def oracle_step(oix, cfg, E, Q, masks, sample, nthreads):
-    """The CPU restatement on `sample` queries of a batch; returns seconds."""
+def oracle_step(oix, cfg, E, Q, masks, sample, nthreads, K=None):
+    """The CPU restatement on `sample` queries of a batch; returns (seconds, ids, scores)."""
     from oracle import oracle as O
     q = Q[:sample].cpu().numpy()
     mk = masks[:sample].cpu().numpy().astype(np.uint32) if masks is not None else None
     t0 = time.time()
-    O.weft_search(oix, q, np.full(sample, 32, np.int32), cfg["nc"], int(E), mk, min(cfg["K"], oix.N),
-                  cfg["k_top"], nthreads=nthreads)
-    return time.time() - t0
+    ids, sc, _ = O.weft_search(oix, q, np.full(sample, 32, np.int32), cfg["nc"], int(E), mk,
+                               min(K or cfg["K"], oix.N), cfg["k_top"], nthreads=nthreads)
+    return time.time() - t0, ids, sc
+
+
+def parity_check(wix, oix, cfg, E, Q, masks, K, sample, oids, osc, nthreads):
+    """Our results for the first `sample` queries of batch Q against the oracle's, stage by
+    stage: Stage-2 probes and scores bit-exact, Stage-3 candidate lists (pids, order and fp32
+    sums) bit-exact, final top-k ids equal except at Stage-4 score ties within 1e-3 (the
+    oracle's own top-k, oids / osc, comes from the timed CPU leg on the same queries)."""
+    from oracle import oracle as O
+    nc, k_top = cfg["nc"], cfg["k_top"]
+    topc, s2, _, _ = wix.centroid_topk(Q, nc)
+    cp, cs, _ = wix.candidates(topc, s2, K, masks=masks)
+    ids, sc = wix.search(Q, nc=nc, K=K, k_top=k_top, masks=masks)
+    topc, s2 = topc[:sample].cpu().numpy(), s2[:sample].cpu().numpy()
+    cp, cs = cp[:sample].cpu().numpy(), cs[:sample].cpu().numpy()
+    ids, sc = ids[:sample].cpu().numpy(), sc[:sample].cpu().numpy()
+    q = Q[:sample].cpu().numpy()
+    mk = masks[:sample].cpu().numpy().astype(np.uint32) if masks is not None else np.zeros(sample, np.uint32)
+    otopc, os2, _ = O.native_prep_batch(q, np.full(sample, 32, np.int32), wix.centroids.cpu().numpy(), nc,
+                                        nthreads=nthreads)
+    s2_ok = bool(np.array_equal(topc, otopc) and np.array_equal(s2.view(np.uint32), os2.view(np.uint32)))
+    s3_ok = True
+    for b in range(sample):
+        op, osum, _ = O.candidates(oix, otopc[b], os2[b], int(E), int(mk[b]), K)
+        s3_ok &= bool(np.array_equal(cp[b], op) and np.array_equal(cs[b].view(np.uint32), osum.view(np.uint32)))
+    a = O.topk_agreement(oix, q, ids, sc, oids, osc, masks=mk, rel_tol=1e-3)
+    return {"queries": sample, "s2_exact": s2_ok, "s3_exact": s3_ok,
+            "top10_ids_equal": a["mismatches"] == 0, "top10_positions_equal": a["equal"],
+            "top10_score_ties": a["ties"], "top10_mismatches": a["mismatches"],
+            "max_rel_score_err": a["max_rel_score_err"],
+            "rule": "Stage 2/3 bit-exact; top-k ids equal except at Stage-4 score ties within 1e-3 relative"}
 
 
 def run_reference(args, cfg, rank, world):
@@ -259,7 +289,7 @@ def run_reference(args, cfg, rank, world):
     oix = host_oracle_index(cents, corp, shard, ix)
     for i in range(args.warmup):
         oracle_step(oix, cfg, ix["E"], Qall[i], masks, sample, nthreads)
-    times = [oracle_step(oix, cfg, ix["E"], Qall[i], masks, sample, nthreads)
+    times = [oracle_step(oix, cfg, ix["E"], Qall[i], masks, sample, nthreads)[0]
              for i in range(args.warmup, args.warmup + args.steps)]
     tot = sum(times)
     v = sample * len(times) / tot
@@ -420,15 +450,17 @@ def run_ours(args, cfg, rank, world, local):
                 "algorithmic": d.get("algorithmic"), "kernel": dom, "peak_source": peak_kind,
                 "timing": "CUDA events at stage boundaries inside the timed region, mean over steps"}
 
-    cpu = None
+    cpu = parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         nthreads = os.cpu_count() or 1
         sample = max(1, min(B, args.cpu_sample or nthreads))
         oix = host_oracle_index(cents, corp, shard, ix)
-        dt = oracle_step(oix, cfg, ix["E"], Q[args.warmup], masks, sample, nthreads)
+        dt, oids, osc = oracle_step(oix, cfg, ix["E"], Q[args.warmup], masks, sample, nthreads, K=K)
         cpu = {"value": sample / dt, "unit": "queries/s", "cores": nthreads, "kind": "port",
                "sample": f"{sample} queries of one batch through all stages ({dt:.1f} s; oracle/weft_oracle.c, "
                          f"OpenMP over queries)"}
+        # parity of the benchmarked configuration: the same queries through our path
+        parity = parity_check(wix, oix, cfg, ix["E"], Q[args.warmup], masks, K, sample, oids, osc, nthreads)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
@@ -445,6 +477,7 @@ def run_ours(args, cfg, rank, world, local):
                        for k, v in stages.items()},
             "stage4_doc_tokens_per_s": stages["s4_maxsim"]["doc_tokens_per_s"],
             "cpu_baseline": cpu,
+            "parity": parity,
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
             "counters": {k: int(v) for k, v in stats.items()},

@@ -100,9 +100,16 @@ int ragrt_centroid_topk(const void* d_Q, const int32_t* d_ntok, int32_t B, int32
  * 32 MiB device array per device instead of cudaMallocAsync/cudaFreeAsync.
  *   - The first call on a device (with it current) looks up the array's address
  *     (cudaGetSymbolAddress; may load the module): make it before any stream capture.
- *   - A call that needs more than 32 MiB of scratch (on the tensor-core path about
- *     B x rows x (520 + NC / 64) bytes at nc = 32, plus 4 bytes per centroid: 17 MB for 256
- *     queries x 32 rows x 65,536 centroids) returns RAGRT_ERR_ARG.
+ *   - A call that needs more than 32 MiB of scratch returns RAGRT_ERR_ARG.  On the
+ *     tensor-core path (kk = nc + impute <= 64) the need is 4 (NC + 1) bytes of centroid
+ *     norms plus, per query row, 8 x (64 S + 1) + 2 ceil(NC / 128) bytes.  S, the number of
+ *     centroid slices (1 to 32), depends on the batch and the SM count: with
+ *     T = ceil(NC / 128) and G = ceil(B x rows / 128),
+ *     S = ceil(T / ceil(T / min(32, T, max(1, SMs / G)))).  Small batches use many slices
+ *     (on 148 SMs, S = 32 up to 4 x 128 rows), batches of more than SMs / 2 x 128 rows use one.
+ *     At 65,536 centroids: 8 queries x 32 rows (S = 32) 4.5 MB, 256 x 32 (S = 2) 17 MB,
+ *     320 x 32 (S = 1) 16 MB; the largest one-slice batch is about 21,500 rows (670 queries
+ *     of 32 rows).
  *   - All calls on a device share the array: calls that overlap on the GPU race.
  * ragrt_centroid_topk_noalloc_error reads (and with reset != 0 clears) the error word that
  * the tensor-core kernel sets when one of its bounded waits gives up (synchronous).
@@ -245,13 +252,13 @@ int ragrt_selftest_wait_timeout(uint32_t polls, void* stream);
 
 /*
  * Merge of the per-shard top-k lists of a doc-sharded search (one process per GPU, corpus split
- * by pid range): d_gathered [world][2][B][k] f32 holds, rank-major as an all-gather leaves
- * them, every rank's scores and global pids (as f32, exact below 2^24; -1 = padding).  Writes
+ * by pid range): d_gathered [world][2][B][k] 32-bit words holds, rank-major as an all-gather
+ * leaves them, every rank's scores (f32 bit patterns) and global pids (int32; -1 = padding).  Writes
  * per query the top k_top by (score desc, pid asc), padding after every real pid of equal score:
  * d_out_ids [B, k_top] int64 (-1 padding), d_out_scores [B, k_top] f32.  No reference
  * counterpart (the reference searches one GPU).
  */
-int ragrt_merge_topk(const float* d_gathered, int32_t world, int32_t B, int32_t k, int32_t k_top,
+int ragrt_merge_topk(const void* d_gathered, int32_t world, int32_t B, int32_t k, int32_t k_top,
                      int64_t* d_out_ids, float* d_out_scores, void* stream);
 
 /* ------------------------------------------------------------------------------------ *

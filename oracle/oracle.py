@@ -179,6 +179,50 @@ def weft_search(index, Q, ntok, nc, n_eids, masks, K, k_top, nthreads=0):
     return ids, sc, st
 
 
+def topk_agreement(index, Q, ids, sc, oids, osc, masks=None, rel_tol=1e-3):
+    """Compare a batch's final top-k (ids int [B, k], scores f32 [B, k]) with the oracle's
+    (oids, osc) under the parity rule of this path:
+
+    * every finite oracle score is matched within `rel_tol` relative (denominator
+      max(|s|, 1)), and the -inf / padding positions coincide;
+    * ids are identical, except at a position where the two differ only because of a
+      Stage-4 tie within tolerance: the oracle's own MaxSim of OUR id there is within
+      2 * rel_tol of the oracle's score at that position (and, for a filtered query, our
+      id passes the filter).
+
+    Returns {"positions", "equal", "ties", "mismatches", "max_rel_score_err"}; a result
+    is in parity when "mismatches" is 0 and "max_rel_score_err" < rel_tol."""
+    ids, sc = np.asarray(ids), np.asarray(sc)
+    oids, osc = np.asarray(oids), np.asarray(osc)
+    Q = _u16(Q)
+    B, k = oids.shape
+    out = {"positions": int(B * k), "equal": 0, "ties": 0, "mismatches": 0, "max_rel_score_err": 0.0}
+    for b in range(B):
+        fin = np.isfinite(osc[b])
+        if not np.array_equal(np.isfinite(sc[b]), fin):
+            out["mismatches"] += int((np.isfinite(sc[b]) != fin).sum())
+        if fin.any():
+            rel = np.abs(sc[b][fin].astype(np.float64) - osc[b][fin]) / np.maximum(np.abs(osc[b][fin]), 1.0)
+            out["max_rel_score_err"] = max(out["max_rel_score_err"], float(rel.max()))
+        mask = int(masks[b]) if masks is not None else 0
+        for i in range(k):
+            if ids[b, i] == oids[b, i]:
+                out["equal"] += 1
+                continue
+            p = int(ids[b, i])
+            ok = 0 <= p < index.N and np.isfinite(osc[b, i])
+            if ok and mask:
+                ok = (int(index.preds[p]) & mask) != 0
+            if ok:
+                s = float(tile_maxsim(index, Q[b], np.array([p], np.int32))[0])
+                ok = abs(s - float(osc[b, i])) <= 2 * rel_tol * max(abs(float(osc[b, i])), 1.0)
+            if ok:
+                out["ties"] += 1
+            else:
+                out["mismatches"] += 1
+    return out
+
+
 def native_prep_batch(Q, ntok, C_, nc, impute=True, nthreads=0):
     Q, C_ = _u16(Q), _u16(C_)
     B = Q.shape[0]

@@ -7,6 +7,7 @@
 //   boff      per centroid and pid range, the first posting with pid >= range start
 //             (postings of a centroid are sorted by pid), so a Stage-3 tile reads only
 //             the sub-list that falls in its pid range.
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -90,6 +91,7 @@ enum : int {
     kBadOffsets = 1 << 3,    // block sums disagree with the lengths
     kBadPids = 1 << 4,       // a pid >= N or pids of a centroid not sorted
     kBadDocs = 1 << 5,       // a passage's tokens are not inside [0, num_tokens)
+    kBadCodes = 1 << 6,      // a doc token's centroid code is outside [0, NC)
 };
 
 // thread per passage: its tokens [doc_offsets[i], doc_offsets[i] + doc_lens[i]) lie inside
@@ -101,6 +103,18 @@ __global__ void k_check_docs(const int64_t* __restrict__ off, const int32_t* __r
     const int64_t o = off[i];
     const int32_t L = lens[i];
     if (o < 0 || L < 0 || o > num_tokens - L) atomicOr(flags, kBadDocs);
+}
+
+// every doc token's code must index a centroid row: Stage 4 gathers centroids[code]
+__global__ void k_check_codes(const int32_t* __restrict__ codes, int64_t num_tokens, int NC,
+                              int* __restrict__ flags) {
+    bool bad = false;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < num_tokens;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int32_t c = codes[i];
+        bad |= (c < 0) | (c >= NC);
+    }
+    if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(flags, kBadCodes);
 }
 
 __global__ void k_list_offsets(const int64_t* __restrict__ bsums, const uint16_t* __restrict__ lengths,
@@ -260,6 +274,9 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
     k_check_rows<<<(unsigned)ceil_div((int64_t)31 * (NC + 1), T), T, 0, stream>>>(d.csr_row_ptrs, NC, flags);
     k_check_docs<<<(unsigned)ceil_div((int64_t)d.num_passages, T), T, 0, stream>>>(d.doc_offsets, d.doc_lens,
                                                                                  d.num_passages, d.num_tokens, flags);
+    if (d.num_tokens > 0)
+        k_check_codes<<<(unsigned)std::min<int64_t>(ceil_div(d.num_tokens, T), (int64_t)num_sms() * 8), T, 0,
+                        stream>>>(d.codes, d.num_tokens, NC, flags);
     if (d.eid_bytes == 1)
         k_centroids<uint8_t><<<(unsigned)ceil_div(NC, T), T, 0, stream>>>(
             d.csr_row_ptrs, (const uint8_t*)d.csr_col_eids, NC, d.num_lists, ix->list_off, ix->cstart, ix->clists, flags);
@@ -273,12 +290,13 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
     if (h_flags) {
         cudaFree(flags);
         return cleanup(fail(RAGRT_ERR_INDEX,
-                            "not a valid plain-IVF index (flags 0x%x:%s%s%s%s%s)", h_flags,
+                            "not a valid plain-IVF index (flags 0x%x:%s%s%s%s%s%s)", h_flags,
                             (h_flags & kBadRow0) ? " row_ptrs row 0 malformed;" : "",
                             (h_flags & kBadRows) ? " subspace rows 1-31 not empty (weft needs a plain-IVF index);" : "",
                             (h_flags & kBadEids) ? " chunk ids of a centroid are not 0..k-1;" : "",
                             (h_flags & kBadOffsets) ? " block sums disagree with lengths / num_postings;" : "",
-                            (h_flags & kBadDocs) ? " doc_offsets / doc_lens reach outside the num_tokens codes;" : ""));
+                            (h_flags & kBadDocs) ? " doc_offsets / doc_lens reach outside the num_tokens codes;" : "",
+                            (h_flags & kBadCodes) ? " a doc token's code is outside [0, num_centroids);" : ""));
     }
     k_check_pids<<<(unsigned)ceil_div((int64_t)NC * 32, T), T, 0, stream>>>(d.csr_packed_24, ix->cstart, ix->clists,
                                                                           d.csr_row_ptrs, ix->list_off, NC,

@@ -144,11 +144,12 @@ int final_topk_launch(const int32_t* pids, const float* scores, int B, int n, co
 }
 
 // ------------------------------------------------------------------ merge over doc shards
-// gathered [world][2][B][k] f32 (rank-major all-gather of every rank's (scores, global pids as
-// f32; pids < 2^24 are exact)) -> per query the top k_top by (score desc, pid asc), padding
-// (pid -1) after every real pid of equal score.  A CTA per query, bitonic sort in shared memory.
+// gathered [world][2][B][k] 32-bit words (rank-major all-gather of every rank's (score as f32
+// bits, global pid as int32; -1 = padding)) -> per query the top k_top by (score desc, pid
+// asc), padding (pid -1) after every real pid of equal score.  A CTA per query, bitonic sort
+// in shared memory.
 __global__ void __launch_bounds__(256)
-merge_shards_topk(const float* __restrict__ gathered, int world, int B, int k, int k_top,
+merge_shards_topk(const uint32_t* __restrict__ gathered, int world, int B, int k, int k_top,
                   int64_t* __restrict__ out_ids, float* __restrict__ out_scores) {
     extern __shared__ uint64_t mkeys[];
     const int b = blockIdx.x;
@@ -157,9 +158,9 @@ merge_shards_topk(const float* __restrict__ gathered, int world, int B, int k, i
         uint64_t key = 0;                                   // sorts after every real entry
         if (i < n) {
             const int r = i / k, j = i % k;
-            const float s = gathered[(((int64_t)r * 2 + 0) * B + b) * k + j];
-            const float pf = gathered[(((int64_t)r * 2 + 1) * B + b) * k + j];
-            const int32_t pid = pf < 0.f ? INT32_MAX : (int32_t)pf;
+            const float s = __uint_as_float(gathered[(((int64_t)r * 2 + 0) * B + b) * k + j]);
+            const int32_t pw = (int32_t)gathered[(((int64_t)r * 2 + 1) * B + b) * k + j];
+            const int32_t pid = pw < 0 ? INT32_MAX : pw;
             key = rank_key(s, pid);
         }
         mkeys[i] = key;
@@ -177,14 +178,14 @@ merge_shards_topk(const float* __restrict__ gathered, int world, int B, int k, i
 
 using namespace ragrt;
 
-extern "C" int ragrt_merge_topk(const float* d_gathered, int32_t world, int32_t B, int32_t k, int32_t k_top,
+extern "C" int ragrt_merge_topk(const void* d_gathered, int32_t world, int32_t B, int32_t k, int32_t k_top,
                                 int64_t* d_out_ids, float* d_out_scores, void* stream) {
     RAGRT_REQUIRE(d_gathered && d_out_ids && d_out_scores, "null argument");
     RAGRT_REQUIRE(world >= 1 && B >= 1 && k >= 1 && k_top >= 1 && k_top <= world * k,
                   "need world, B, k >= 1 and 1 <= k_top <= world * k");
     RAGRT_REQUIRE((int64_t)world * k <= 8192, "at most 8,192 entries per query");
     const size_t smem = sizeof(uint64_t) * next_pow2(world * k);
-    merge_shards_topk<<<B, 256, smem, (cudaStream_t)stream>>>(d_gathered, world, B, k, k_top, d_out_ids, d_out_scores);
+    merge_shards_topk<<<B, 256, smem, (cudaStream_t)stream>>>((const uint32_t*)d_gathered, world, B, k, k_top, d_out_ids, d_out_scores);
     RAGRT_LAUNCH_CHECK();
     return RAGRT_OK;
 }

@@ -38,13 +38,16 @@ def slice_docs(doc_offsets, doclens, codes, residuals, preds, lo, hi):
 
 def gather_topk(ids, scores, world, pid_base, group=None):
     """ids int32 [B, k] (local pids, -1 padding), scores f32 [B, k] (-inf padding) on this rank
-    -> every rank's list, rank-major, as f32 [world * 2, B, k] (scores, then global pids; pids
-    < 2^24 are exact in fp32, padding stays -1), with one all_gather_into_tensor."""
+    -> every rank's list, rank-major, as int32 words [world * 2, B, k]: the scores' f32 bit
+    patterns, then the global pids (-1 padding), with one all_gather_into_tensor.  The pids
+    travel as integers, so every pid below 2^31 arrives exactly."""
     import torch.distributed as dist
     gpid = torch.where(ids >= 0, ids.to(torch.int64) + pid_base, torch.full_like(ids, -1, dtype=torch.int64))
-    pack = torch.stack([scores.to(torch.float32), gpid.to(torch.float32)], 0)
-    out = torch.empty(world * 2, *pack.shape[1:], dtype=pack.dtype, device=pack.device)
-    dist.all_gather_into_tensor(out, pack, group=group)
+    if pid_base + (1 << 24) >= 2 ** 31:
+        raise RuntimeError("global pids must stay below 2^31")
+    pack = torch.stack([scores.to(torch.float32).contiguous().view(torch.int32), gpid.to(torch.int32)], 0)
+    out = torch.empty(world * 2, *pack.shape[1:], dtype=torch.int32, device=pack.device)
+    dist.all_gather_into_tensor(out, pack.contiguous(), group=group)
     return out
 
 
@@ -84,28 +87,37 @@ def gather_probes(topc, scores, world, B, group=None):
     return t, s
 
 
-def sharded_search(wix, Q, world, rank, pid_base, nc=32, K=4096, k_top=10, masks=None, events=None, group=None):
+def sharded_search(wix, Q, world, rank, pid_base, nc=32, K=4096, k_top=10, ntok=None, masks=None, events=None,
+                   group=None):
     """The `weft` search of a query batch Q [B, 32, 128] fp16 over a corpus split by doc range:
     Stage 2 on this rank's query slice, probe lists all-gathered, Stages 1-4 and the top-k on
-    this rank's shard `wix` (local pids + pid_base), then the merge over ranks.  Returns
-    (global pids int64 [B, k_top], scores f32 [B, k_top]), the same on every rank.  `events`:
-    optional 5 torch.cuda.Event recorded before Stage 2, after the probe exchange, after
-    Stages 1-3, after Stage 4 and after the local top-k."""
+    this rank's shard `wix` (local pids + pid_base), then the merge over ranks.  `ntok` (int32
+    [B], optional) limits the query tokens of Stages 2-3 as in WeftIndex.search; Stage 4 scores
+    all 32 rows of Q, as the single-GPU search does.  Returns (global pids int64 [B, k_top],
+    scores f32 [B, k_top]), the same on every rank.  `events`: optional 5 torch.cuda.Event
+    recorded before Stage 2, after the probe exchange, after Stages 1-3, after Stage 4 and
+    after the local top-k."""
     def mark(i):
         if events is not None:
             events[i].record()
     B = Q.shape[0]
     lo, hi, per = query_slice(B, world, rank)
+    nts = None
     if hi - lo == per:
         Qs = Q[lo:hi]
+        if ntok is not None:
+            nts = ntok[lo:hi]
     else:                                        # the last slice of a batch that world does not divide
         Qs = Q.new_zeros(per, *Q.shape[1:])
         Qs[:hi - lo] = Q[lo:hi]
+        if ntok is not None:                     # padding queries: full length, results dropped
+            nts = torch.full((per,), 32, dtype=ntok.dtype, device=ntok.device)
+            nts[:hi - lo] = ntok[lo:hi]
     mark(0)
-    topc, sc, _, _ = wix.centroid_topk(Qs, nc)
+    topc, sc, _, _ = wix.centroid_topk(Qs, nc, ntok=nts)
     topc, sc = gather_probes(topc, sc, world, B, group=group)
     mark(1)
-    pids, _, _ = wix.candidates(topc, sc, K, masks=masks)
+    pids, _, _ = wix.candidates(topc, sc, K, ntok=ntok, masks=masks)
     mark(2)
     f = wix.tile_maxsim(Q, pids)
     mark(3)

@@ -40,7 +40,9 @@ def small_corpus(num_docs=300, num_centres=64, subs=8, seed=0, len_range=(8, 60)
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("RAGRT_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get(
+        "RAGRT_REFERENCE_DIR", os.path.join(os.path.dirname(REPO), "reference")),
+        help="the reference source tree (default: RAGRT_REFERENCE_DIR, else `reference` beside this repository)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "src"))
     import weft_prep as RW                   # the reference's own modules

@@ -215,6 +215,21 @@ def test_documents_outside_the_codes_are_rejected():
         mk(bad, E)
 
 
+@pytest.mark.parametrize("bad_code", [-1, "NC"])
+def test_codes_outside_the_centroids_are_rejected(bad_code):
+    """A doc token whose centroid code is not a row of the bound centroids fails at bind time,
+    so neither rerank mode ever gathers outside the centroid table."""
+    d, Q, E, _ = small_corpus()
+    from ragrt_b200._lib import RagrtError
+    from tests.helpers import weft_index as mk
+    bad = dict(d)
+    codes = d["codes"].clone()
+    codes[len(codes) // 2] = -1 if bad_code == -1 else d["centroids"].shape[0]
+    bad["codes"] = codes
+    with pytest.raises(RagrtError, match="code is outside"):
+        mk(bad, E)
+
+
 @pytest.mark.parametrize("nq,ntok_drop", [(8, 0), (5, 7)])
 def test_stage2_tensor_core_many_tiles(nq, ntok_drop):
     """Stage 2 with several 128-row tiles and centroid slices (the tcgen05 path) is bit-exact."""

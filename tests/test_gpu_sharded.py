@@ -151,27 +151,36 @@ def test_sharded_search_single_rank_equals_search(zipf_corpus):
     port = s.getsockname()[1]
     s.close()
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    # ragged query lengths go through the sharded path as through WeftIndex.search
+    ntok = torch.tensor([32 - 5 * (b % 4) for b in range(Qc.shape[0])], dtype=torch.int32, device="cuda")
     try:
         ids, sc = shard.sharded_search(wix, Qc, 1, 0, pb, nc=32, K=400, k_top=10)
+        rids_nt, rsc_nt = shard.sharded_search(wix, Qc, 1, 0, pb, nc=32, K=400, k_top=10, ntok=ntok)
     finally:
         dist.destroy_process_group()
     rids, rsc = wix.search(Qc, nc=32, K=400, k_top=10)
     assert torch.equal(ids, rids.to(torch.int64)) and torch.equal(sc, rsc)
+    nids, nsc = wix.search(Qc, nc=32, K=400, k_top=10, ntok=ntok)
+    assert torch.equal(rids_nt, nids.to(torch.int64)) and torch.equal(rsc_nt, nsc)
 
 
-@pytest.mark.parametrize("world,k,k_top", [(8, 10, 10), (3, 7, 12), (1, 10, 5)])
-def test_merge_kernel_orders_like_the_rule(world, k, k_top):
+@pytest.mark.parametrize("world,k,k_top,pid_hi", [(8, 10, 10, 5000), (3, 7, 12, 5000), (1, 10, 5, 5000),
+                                                  (8, 10, 10, 1 << 27)])
+def test_merge_kernel_orders_like_the_rule(world, k, k_top, pid_hi):
     """ragrt_merge_topk: (score desc, pid asc), padding (-1) after real pids of equal score --
-    ties, -inf scores and padding included."""
+    ties, -inf scores and padding included; global pids past 2^24 (8 shards of up to 2^24
+    passages each) come back exactly."""
     from ragrt_b200 import _lib
     from ragrt_b200.weft import _ptr, _stream
     g = np.random.default_rng(world * 100 + k)
     B = 16
     sc = g.choice(np.array([0.5, 0.25, 1.0, -np.inf, 2.0], np.float32), size=(world, B, k))
-    pid = g.integers(0, 5000, size=(world, B, k)).astype(np.float32)
+    pid = g.integers(0, pid_hi, size=(world, B, k)).astype(np.int32)
+    if pid_hi > (1 << 24):
+        pid[:, :, 0] = (1 << 24) + 1 + 2 * np.arange(B)[None, :]      # odd: not representable in fp32
     pad = g.random((world, B, k)) < 0.2
-    pid[pad], sc[pad] = -1.0, -np.inf
-    gathered = torch.from_numpy(np.stack([sc, pid], 1).astype(np.float32)).cuda()     # [world, 2, B, k]
+    pid[pad], sc[pad] = -1, -np.inf
+    gathered = torch.from_numpy(np.stack([sc.view(np.int32), pid], 1)).cuda()        # [world, 2, B, k] words
     ids = torch.empty(B, k_top, dtype=torch.int64, device="cuda")
     out = torch.empty(B, k_top, dtype=torch.float32, device="cuda")
     _lib.check(_lib.lib().ragrt_merge_topk(_ptr(gathered), world, B, k, k_top, _ptr(ids), _ptr(out), _stream()))

@@ -61,10 +61,11 @@ def _worker(rank, world, port, q):
 
 
 def _merge_rule(gathered, world, B, k_top):
-    """The merge rule applied to gather_topk's output f32 [world * 2, B, k] with torch sorts:
-    score desc, then pid asc, padding (-1) after every real pid of equal score."""
+    """The merge rule applied to gather_topk's output int32 words [world * 2, B, k] (score bits,
+    global pids) with torch sorts: score desc, then pid asc, padding (-1) after every real pid
+    of equal score."""
     out = gathered.view(world, 2, B, -1)
-    sc = out[:, 0].permute(1, 0, 2).reshape(B, -1)
+    sc = out[:, 0].permute(1, 0, 2).reshape(B, -1).contiguous().view(torch.float32)
     pid = out[:, 1].permute(1, 0, 2).reshape(B, -1).to(torch.int64)
     key = torch.where(pid >= 0, pid, torch.full_like(pid, 1 << 40))
     order = torch.argsort(key, dim=1, stable=True)                       # pid asc ...

@@ -76,6 +76,21 @@ def test_noalloc_matches_allocating_entry_point_twice():
     assert L.ragrt_centroid_topk_noalloc_error(1) == 0
 
 
+def test_noalloc_slice_layouts_in_a_row():
+    """The tensor-core path lays its per-row lists out by slice count, which follows the batch
+    size: 4 queries (one 128-row block) split 8,192 centroids into 32 slices, 320 queries (80
+    row blocks on 148 SMs) use a single slice.  Calls with the two layouts back to back, each
+    against the allocating entry point bit for bit, show that no region of the shared array
+    carries a previous layout's contents into the next call."""
+    cases = [(4, 8192, 32, True, True, 41), (320, 8192, 32, True, True, 43), (4, 8192, 32, True, False, 47)]
+    for B, NC, nc, impute, ragged, seed in cases:
+        Q, ntok, Cm = _inputs(B, NC, seed, ragged)
+        ref = _call("ragrt_centroid_topk", Q, ntok, Cm, nc, impute)
+        got = _call("ragrt_centroid_topk_noalloc", Q, ntok, Cm, nc, impute)
+        _same(ref, got)
+    assert _lib.lib().ragrt_centroid_topk_noalloc_error(1) == 0
+
+
 def test_noalloc_rejects_oversized_scratch():
     L = _lib.lib()
     Q, _, Cm = _inputs(4, 2048, 5, False)
