@@ -218,13 +218,27 @@ int ragrt_weft_search_profiled(ragrt_index* index, const void* d_Q, const int32_
 /*
  * Counters accumulated over calls since the last reset (the reference's drop stats,
  * ragrt_fused_kernel.cu:33-47, :884-899): out[0] queries, out[1] postings scanned
- * (sum over kept (token, probe) pairs of list length), out[2] distinct postings read
- * (each probed list once per query), out[3] passages touched, out[4] kept probes,
- * out[5] candidates reranked.  Synchronises the device.  out[2] needs one extra kernel per
- * Stage-3 pass and is counted only after ragrt_index_count_distinct(index, 1) (off by default).
+ * (sum over kept (token, probe) pairs of list length: the reference's ST_POSTINGS),
+ * out[2] distinct postings read (each probed list once per query: what Stage 3 walks),
+ * out[3] passages touched, out[4] kept probes, out[5] candidates reranked, out[6] tasks
+ * (sum over kept probes of their chunk lists below n_eids: the reference's ST_TASKS),
+ * out[7] pid-range blocks that Stage 3 found too dense for its walk-once table and handed
+ * to the per-token kernel (no reference counterpart).  Synchronises the device.
+ * ragrt_index_count_distinct is kept for compatibility: every counter is always counted (the
+ * distinct lists are a by-product of Stage 3).
  */
 int ragrt_index_count_distinct(ragrt_index* index, int32_t enable);
-#define RAGRT_NUM_STATS 6
+
+/*
+ * Stage-3 algorithm of an index (the reference's set_stage3_mode, optix_corr_torch_3d.cpp:941-943,
+ * selects among its sort- and hash-based Stage 3 the same way): 0 (default) walks every distinct
+ * probed list of a query once per pid range and hands ranges too dense for its per-passage
+ * table to the per-token kernel; 1 runs the per-token kernel on every range.  Both give
+ * bit-identical candidates.  range_passages sets the walk's pid-range width (rounded down to a
+ * multiple of the index's range-offset granularity, at least one granule); 0 chooses it.
+ */
+int ragrt_index_set_stage3_mode(ragrt_index* index, int32_t mode, int32_t range_passages);
+#define RAGRT_NUM_STATS 8
 int ragrt_index_stats(ragrt_index* index, uint64_t* out, int32_t reset);
 
 /* Message of the last failing call on this thread ("" if none). */

@@ -20,8 +20,9 @@ U32 = C.c_uint32
 ERR_NAMES = {-1: "RAGRT_ERR_ARG", -2: "RAGRT_ERR_CUDA", -3: "RAGRT_ERR_CAPACITY", -4: "RAGRT_ERR_INDEX",
              -5: "RAGRT_ERR_UNSUPPORTED", -6: "RAGRT_ERR_DEVICE"}
 
-NUM_STATS = 6
-STAT_NAMES = ("queries", "postings", "distinct_postings", "touched", "probes", "candidates")
+NUM_STATS = 8
+STAT_NAMES = ("queries", "postings", "distinct_postings", "touched", "probes", "candidates", "tasks",
+              "dense_ranges")
 
 
 class IndexDesc(C.Structure):
@@ -49,6 +50,7 @@ _SIGS = {
     "ragrt_weft_search_profiled": (I32, [P, P, P, I32, I32, I32, P, I32, I32, I32, P, P, P, P]),
     "ragrt_index_stats": (I32, [P, C.POINTER(C.c_uint64), I32]),
     "ragrt_index_count_distinct": (I32, [P, I32]),
+    "ragrt_index_set_stage3_mode": (I32, [P, I32, I32]),
     "ragrt_last_error": (C.c_char_p, []),
     "ragrt_version": (C.c_char_p, []),
     "ragrt_launch_count": (C.c_uint64, []),

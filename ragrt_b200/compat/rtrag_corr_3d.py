@@ -83,9 +83,13 @@ def reset_drop_stats():
 
 
 def get_drop_stats():
-    """Counters since the last reset (all zero unless set_drop_stats(True)).  Kept: launches
-    (queries), rays (tokens x 32), tasks (kept probes), postings (postings scanned); the RT /
-    codebook counters stay 0 in the weft configuration."""
+    """Counters since the last reset (all zero unless set_drop_stats(True)), with the
+    reference's meaning (ragrt_fused_kernel.cu:33-47): launches (queries), rays (tokens x 32
+    subspaces), tasks (posting lists of the kept (token, probe) pairs, ST_TASKS) and postings
+    (their postings, ST_POSTINGS), the last two read from the index's device counters after
+    each search while the stats are on (one device synchronisation per call, as the reference
+    asks to leave stats off for timing).  The RT / codebook counters stay 0 in the weft
+    configuration."""
     return dict(_stats)
 
 
@@ -228,6 +232,15 @@ class CorrIndex3D:
     def _n_eids(self, k_eids):
         return min(int(k_eids), self.E)
 
+    def _stats_begin(self):
+        if _knobs["stats"]:
+            self._ix.stats(reset=True)             # drop what calls made with the stats off counted
+
+    def _stats_end(self):
+        if _knobs["stats"]:
+            st = self._ix.stats(reset=True)
+            _record(tasks=st["tasks"], postings=st["postings"])
+
     def _candidates(self, topc, scores, k_cent, k_candidates, query_mask, k_eids, ntok=None):
         full = not _knobs["compact_scores"]
         if topc.dim() == 2:
@@ -236,8 +249,11 @@ class CorrIndex3D:
         masks = torch.full((topc.shape[0],), int(query_mask) & 0xFFFFFFFF, dtype=torch.int64,
                            device=topc.device).to(torch.int32) if query_mask else None
         try:
-            return self._ix.candidates(topc, scores, k_candidates, ntok=ntok, masks=masks,
-                                       n_eids=self._n_eids(k_eids), full_scores=full)
+            self._stats_begin()
+            out = self._ix.candidates(topc, scores, k_candidates, ntok=ntok, masks=masks,
+                                      n_eids=self._n_eids(k_eids), full_scores=full)
+            self._stats_end()
+            return out
         except RagrtError as e:
             raise RuntimeError(str(e)) from None
 
@@ -325,8 +341,13 @@ class CorrIndex3D:
             masks = torch.full((B,), int(query_mask) & 0xFFFFFFFF, dtype=torch.int64,
                                device=Q_fp16.device).to(torch.int32)
         try:
-            return self._ix.search(Q_fp16, nc=k_cent, K=k_candidates, k_top=k_top, ntok=ntok, masks=masks,
-                                   rerank="tc" if _knobs["rerank"] == "wmma" else "simt")
+            self._stats_begin()
+            out = self._ix.search(Q_fp16, nc=k_cent, K=k_candidates, k_top=k_top, ntok=ntok, masks=masks,
+                                  rerank="tc" if _knobs["rerank"] == "wmma" else "simt")
+            self._stats_end()
+            n = int(ntok.sum()) if ntok is not None else 32 * B
+            _record(launches=B, rays=n * _NUM_SUBSPACES)
+            return out
         except RagrtError as e:
             raise RuntimeError(str(e)) from None
 

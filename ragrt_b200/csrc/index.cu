@@ -338,6 +338,15 @@ extern "C" int ragrt_index_count_distinct(ragrt_index* ix, int32_t enable) {
     return RAGRT_OK;
 }
 
+extern "C" int ragrt_index_set_stage3_mode(ragrt_index* ix, int32_t mode, int32_t range_passages) {
+    RAGRT_REQUIRE(ix, "null index");
+    RAGRT_REQUIRE(mode == 0 || mode == 1, "stage-3 mode must be 0 (walk-once) or 1 (per-token)");
+    RAGRT_REQUIRE(range_passages >= 0 && range_passages <= (1 << 20), "range_passages must be in [0, 2^20]");
+    ix->s3_mode = mode;
+    ix->s3_range = range_passages;
+    return RAGRT_OK;
+}
+
 extern "C" int ragrt_index_stats(ragrt_index* ix, uint64_t* out, int32_t reset) {
     RAGRT_REQUIRE(ix, "null index");
     if (out) {

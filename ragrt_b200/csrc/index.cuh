@@ -25,7 +25,9 @@ struct ragrt_index {
 
     ragrt_workspace ws;
     unsigned long long* stats = nullptr;   // [RAGRT_NUM_STATS]
-    int count_distinct = 0;                // count out[2] (one extra kernel per Stage-3 pass)
+    int count_distinct = 0;                // kept for the ABI; out[2] is always counted
+    int s3_mode = 0;                       // 0 walk-once (+ per-token for dense ranges), 1 per-token only
+    int s3_range = 0;                      // passages per walk-once range (0: automatic)
 };
 
 namespace ragrt {

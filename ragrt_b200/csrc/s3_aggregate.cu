@@ -61,6 +61,11 @@ struct S3Params {
     unsigned long long* pool_count;   // [nq]
     unsigned int* work;          // work counter
     unsigned long long* stats;
+    // queue mode: the work items are the pid-range blocks the walk deferred, (qi << 32 | block),
+    // block b covering index ranges [b * m, b * m + m); their number is read on the device
+    const unsigned long long* dense;
+    const unsigned int* dense_count;
+    int m;
 };
 
 __device__ __forceinline__ uint16_t f2h_pos15(float base) {
@@ -89,7 +94,7 @@ s3_accumulate(S3Params p) {
     unsigned long long st_post = 0, st_probes = 0;
     int cached_q = -1;
     const unsigned nrb = ((unsigned)p.R + p.rpj - 1) / p.rpj;
-    const unsigned total_jobs = (unsigned)p.nq * nrb;
+    const unsigned total_jobs = p.dense ? *p.dense_count : (unsigned)p.nq * nrb;
     __syncthreads();
 
     for (;;) {
@@ -97,8 +102,17 @@ s3_accumulate(S3Params p) {
         __syncthreads();
         const unsigned job = s_unit;
         if (job >= total_jobs) break;
-        const int qi = (int)(job / nrb);
-        const int r0 = (int)(job % nrb) * p.rpj, r1 = min(p.R, r0 + p.rpj);
+        int qi, r0, r1;
+        if (p.dense) {
+            const unsigned long long d = p.dense[job];
+            qi = (int)(d >> 32);
+            r0 = (int)(d & 0xFFFFFFFFu) * p.m;
+            r1 = min(p.R, r0 + p.m);
+        } else {
+            qi = (int)(job / nrb);
+            r0 = (int)(job % nrb) * p.rpj;
+            r1 = min(p.R, r0 + p.rpj);
+        }
       for (int r = r0; r < r1; ++r) {
         const int q = p.q0 + qi;
         const uint32_t mask = p.masks ? p.masks[q] : 0u;
@@ -267,42 +281,6 @@ s3_accumulate(S3Params p) {
     }
 }
 
-// per query: distinct probed lists and their postings (the roofline's P_lists)
-__global__ void s3_query_lists(S3Params p, unsigned long long* __restrict__ distinct_postings) {
-    __shared__ int s_ids[kRows * RAGRT_MAX_PROBE];
-    __shared__ unsigned s_n;
-    const int q = p.q0 + blockIdx.x;
-    const int nt = p.ntok ? min(p.ntok[q], p.rows) : p.rows;
-    if (threadIdx.x == 0) s_n = 0;
-    __syncthreads();
-    for (int i = threadIdx.x; i < nt * p.kc; i += blockDim.x) {
-        const int t = i / p.kc, j = i % p.kc;
-        const int c = p.topc[((int64_t)q * p.rows + t) * p.kc + j];
-        if (c < 0 || c >= p.NC) continue;
-        const float base = p.full_scores ? p.scores[((int64_t)q * p.rows + t) * p.NC + c]
-                                         : p.scores[((int64_t)q * p.rows + t) * p.kc + j];
-        if (base > 0.0f) s_ids[atomicAdd(&s_n, 1u)] = c;
-    }
-    __syncthreads();
-    const unsigned n = s_n;
-    unsigned long long tot = 0;
-    for (unsigned i = threadIdx.x; i < n; i += blockDim.x) {
-        const int c = s_ids[i];
-        bool first = true;
-        for (unsigned k = 0; k < i; ++k)
-            if (s_ids[k] == c) { first = false; break; }
-        if (first) {
-            const int nl = min(p.clists[c], p.n_eids);
-            tot += nl > 0 ? (unsigned long long)(p.list_off[p.rp[c] + nl] - p.cstart[c]) : 0ull;
-        }
-    }
-    for (int o = 16; o; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
-    if ((threadIdx.x & 31) == 0 && tot) {
-        atomicAdd(&distinct_postings[blockIdx.x], tot);
-        if (p.stats) atomicAdd(&p.stats[2], tot);
-    }
-}
-
 }  // namespace ragrt
 
 using namespace ragrt;
@@ -311,8 +289,10 @@ namespace ragrt {
 
 size_t s3_workspace_bytes(const ragrt_index* ix, int nq_sub) {
     return sizeof(uint64_t) * (size_t)nq_sub * ix->d.num_passages        // pool
-           + sizeof(unsigned long long) * (size_t)nq_sub * 2            // pool counts, distinct postings
-           + 256;
+           + sizeof(unsigned long long) * (size_t)nq_sub                // pool counts
+           + 256                                                          // work counters, queue count
+           + s3_walk_lists_bytes(nq_sub, kRows * RAGRT_MAX_PROBE)        // distinct lists per query
+           + s3_walk_dense_bytes(ix, nq_sub) + 1024;                     // deferred range blocks
 }
 
 int s3_max_sub_batch(const ragrt_index* ix, int B) {
@@ -325,6 +305,8 @@ int s3_max_sub_batch(const ragrt_index* ix, int B) {
     return (int)std::min<int64_t>(sub, B);
 }
 
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
 int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_scores, const int32_t* ntok, int B,
            int rows, int kc, int n_eids, const uint32_t* masks, int K, int32_t* cand_pids, float* cand_sums,
            int64_t* num_touched, void* ws, size_t ws_bytes, cudaStream_t stream) {
@@ -334,10 +316,14 @@ int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_s
     const int W = 1 << ix->w_shift;
     char* wsp = (char*)ws;
     uint64_t* pool = (uint64_t*)wsp;
-    wsp += sizeof(uint64_t) * (size_t)sub * ix->d.num_passages;
-    unsigned long long* counts = (unsigned long long*)wsp;        // [sub] pool counts, [sub] distinct postings
-    wsp += sizeof(unsigned long long) * (size_t)sub * 2;
-    unsigned int* work = (unsigned int*)wsp;
+    wsp += align256(sizeof(uint64_t) * (size_t)sub * ix->d.num_passages);
+    unsigned long long* counts = (unsigned long long*)wsp;        // [sub] pool counts
+    wsp += align256(sizeof(unsigned long long) * (size_t)sub);
+    unsigned int* ctr = (unsigned int*)wsp;                       // [0] walk work, [1] queue work, [2] queue count
+    wsp += 256;
+    void* lists = wsp;
+    wsp += align256(s3_walk_lists_bytes(sub, rows * kc));
+    unsigned long long* dense = (unsigned long long*)wsp;
 
     const size_t smem = sizeof(unsigned long long) * W + sizeof(uint32_t) * kS3Warps * (W >> 5) +
                         (sizeof(int64_t) + 2 * sizeof(int32_t) + sizeof(uint16_t)) * kRows * kc + 16;
@@ -348,7 +334,15 @@ int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_s
     per_sm = std::max(1, per_sm);
     for (int q0 = 0; q0 < B; q0 += sub) {
         const int nq = std::min(sub, B - q0);
-        RAGRT_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(unsigned long long) * 2 * sub + 16, stream));
+        RAGRT_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(unsigned long long) * sub, stream));
+        RAGRT_CUDA_TRY(cudaMemsetAsync(ctr, 0, 16, stream));
+        const uint32_t* mk = ix->d.doc_predicates ? masks : nullptr;   // no predicates bound: no filter
+        // 1. every distinct probed list walked once per pid range; dense ranges are queued
+        int rc = s3_walk_run(ix, topc, scores, full_scores, ntok, q0, nq, rows, kc, n_eids, mk, pool, counts,
+                             ctr + 0, dense, ctr + 2, lists, stream);
+        if (rc) return rc;
+        // 2. the queued ranges by the per-token kernel (no per-passage rows; exits at once when
+        //    the queue is empty)
         S3Params p;
         p.packed = ix->d.csr_packed_24;
         p.preds = ix->d.doc_predicates;
@@ -368,32 +362,24 @@ int s3_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_s
         p.rows = rows;
         p.kc = kc;
         p.ntok = ntok;
-        p.masks = masks;
+        p.masks = mk;
         p.q0 = q0;
         p.nq = nq;
+        p.rpj = 1;
         p.pool = pool;
         p.pool_cap = ix->d.num_passages;
         p.pool_count = counts;
-        p.work = work;
-        p.stats = ix->stats;
-        if (masks && !ix->d.doc_predicates) p.masks = nullptr;   // no predicates bound: no filter
-        // 8 ranges per work item (the probe table is built once per item), halved while the
-        // items would give the persistent CTAs fewer than 8 each (small shards): the last
-        // round of a few large items leaves CTAs idle
-        const int64_t ctas = (int64_t)per_sm * num_sms();
-        int rpj = kS3RangesPerJob;
-        while (rpj > 1 && (int64_t)nq * ((ix->num_ranges + rpj - 1) / rpj) < 8 * ctas) rpj >>= 1;
-        p.rpj = rpj;
-        const int64_t jobs = (int64_t)nq * ((ix->num_ranges + rpj - 1) / rpj);
-        const int grid = (int)std::min<int64_t>(jobs, ctas);
+        p.work = ctr + 1;
+        p.stats = nullptr;                    // the statistics are counted once, by the walk's prep
+        p.dense = dense;
+        p.dense_count = ctr + 2;
+        p.m = s3_walk_ranges(ix);
+        const int grid = (int)std::min<int64_t>((int64_t)per_sm * num_sms(),
+                                                (int64_t)nq * ceil_div(ix->num_ranges, p.m));
         s3_accumulate<<<grid, kS3Threads, smem, stream>>>(p);
         RAGRT_LAUNCH_CHECK();
-        if (ix->count_distinct) {             // statistics only: not needed for the result
-            s3_query_lists<<<nq, 256, 0, stream>>>(p, counts + sub);
-            RAGRT_LAUNCH_CHECK();
-        }
-        int rc = s3_select_launch(pool, ix->d.num_passages, counts, q0, nq, K, cand_pids, cand_sums, num_touched,
-                                  ix->stats, stream);
+        rc = s3_select_launch(pool, ix->d.num_passages, counts, q0, nq, K, cand_pids, cand_sums, num_touched,
+                              ix->stats, stream);
         if (rc) return rc;
     }
     return RAGRT_OK;

@@ -114,6 +114,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--rerank", default="tc", choices=("tc", "simt"))
+    ap.add_argument("--s3-mode", type=int, default=0, choices=(0, 1),
+                    help="Stage 3: 0 walk-once (per-token for dense ranges), 1 per-token only")
+    ap.add_argument("--s3-range", type=int, default=0, help="Stage 3 walk range width in passages (0: auto)")
     a = ap.parse_args()
     dev = "cuda"
     t0 = time.time()
@@ -133,18 +136,17 @@ def main():
                         C, corp["bucket_weights"], corp["reversed_bit_map"], corp["decomp_table"], E=ix["E"])
         print(f"corpus ready in {time.time() - t0:.1f} s", file=sys.stderr)
         if "s3" in stages:
+            wix.set_stage3_mode(a.s3_mode, a.s3_range)
             topc, sc, _, _ = centroid_topk(Q, C, a.nc)
             ms = timed(lambda: wix.candidates(topc, sc, a.K), a.steps, a.warmup)
-            wix.count_distinct(True)          # work counts from one more, untimed pass
-            wix.stats(reset=True)
+            wix.stats(reset=True)             # work counts from one more, untimed pass
             wix.candidates(topc, sc, a.K)
             st = wix.stats()
-            wix.count_distinct(False)
-            n = 1
-            b = (3.0 * st["distinct_postings"] + 8.0 * st["touched"]) / n
-            out.append({"stage": "s3", "ms": ms, "gbs": b / ms / 1e6, "postings_per_query": st["postings"] / n / a.batch,
-                        "distinct_postings_per_query": st["distinct_postings"] / n / a.batch,
-                        "touched_per_query": st["touched"] / n / a.batch})
+            b = 3.0 * st["distinct_postings"] + 8.0 * st["touched"]
+            out.append({"stage": "s3", "s3_mode": a.s3_mode, "s3_range": a.s3_range, "ms": ms, "gbs": b / ms / 1e6,
+                        "postings_per_query": st["postings"] / a.batch,
+                        "distinct_postings_per_query": st["distinct_postings"] / a.batch,
+                        "touched_per_query": st["touched"] / a.batch, "dense_ranges": st["dense_ranges"]})
         if "s4" in stages:
             cand = synth.random_candidates(a.docs, a.batch, a.K, seed=0, device=dev)
             mode = 1 if a.rerank == "tc" else 0

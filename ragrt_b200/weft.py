@@ -312,13 +312,21 @@ class WeftIndex:
         return pc, tc
 
     def count_distinct(self, enable=True):
-        """Count distinct postings per query in stats() (one extra kernel per Stage-3 pass; off
-        by default)."""
+        """Kept for compatibility: distinct postings are always counted (Stage 3 finds each
+        query's distinct lists anyway)."""
         _lib.check(_lib.lib().ragrt_index_count_distinct(self.handle, int(bool(enable))))
 
+    def set_stage3_mode(self, mode, range_passages=0):
+        """0 (default): walk each distinct probed list once per pid range (ranges too dense for
+        the walk go to the per-token kernel); 1: the per-token kernel on every range.  Results
+        are bit-identical.  range_passages: the walk's pid-range width (0: automatic)."""
+        _lib.check(_lib.lib().ragrt_index_set_stage3_mode(self.handle, int(mode), int(range_passages)))
+
     def stats(self, reset=False):
-        """Counters since the last reset: queries, postings (scanned), distinct_postings (only
-        while count_distinct is on), touched, probes, candidates."""
+        """Counters since the last reset: queries, postings (scanned per kept (token, probe),
+        the reference's ST_POSTINGS), distinct_postings (each probed list once per query),
+        touched, probes (kept), candidates, tasks (the reference's ST_TASKS), dense_ranges (pid-range
+        blocks Stage 3 handed from its walk-once kernel to the per-token one)."""
         buf = (C.c_uint64 * _lib.NUM_STATS)()
         _lib.check(_lib.lib().ragrt_index_stats(self.handle, buf, int(bool(reset))))
         return dict(zip(_lib.STAT_NAMES, list(buf)))

@@ -102,6 +102,35 @@ def test_candidates_and_filter(setup, mask):
         assert bool(((g["doc_predicates"][kept] & mask) != 0).all())
 
 
+def test_drop_stats_count_postings_and_tasks(setup):
+    """get_drop_stats() reports the reference's counters for the weft path: launches, rays,
+    tasks (posting lists of the kept (token, probe) pairs) and postings (their postings),
+    equal to the oracle's counts for the same queries; all zero while the stats are off."""
+    d, g, Q, E, idx = setup
+    oix = oracle_index(d)
+    R.set_drop_stats(False)
+    R.reset_drop_stats()
+    a = _query_args(g, Q[0])
+    idx.candidates(a[2], a[3], a[4], NC, K, 0, E)
+    assert all(v == 0 for v in R.get_drop_stats().values())
+    R.set_drop_stats(True)
+    try:
+        exp_post = exp_tasks = 0
+        for b in range(2):
+            a = _query_args(g, Q[b])
+            idx.candidates(a[2], a[3], a[4], NC, K, 0, E)
+            _, _, st = O.candidates(oix, a[3].cpu().numpy(), a[4].cpu().numpy(), E, 0, K)
+            exp_post += st["postings"]
+            exp_tasks += st["tasks"]
+        got = R.get_drop_stats()
+        assert got["launches"] == 2 and got["rays"] == 2 * 32 * 32
+        assert got["postings"] == exp_post and got["tasks"] == exp_tasks, (got, exp_post, exp_tasks)
+        assert exp_post > 0
+    finally:
+        R.set_drop_stats(False)
+        R.reset_drop_stats()
+
+
 def test_search_batch_entry(setup):
     d, g, Q, E, idx = setup
     wix = weft_index(d, E)

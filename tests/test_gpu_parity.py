@@ -85,6 +85,27 @@ def test_stage3_bit_exact(corpus, K, mask):
         assert np.array_equal(sums[b].view(np.uint32), os_.view(np.uint32)), f"query {b}: sums differ"
 
 
+@pytest.mark.parametrize("mask,range_passages", [(0, 0), (2, 0), (0, 8192)])
+def test_stage3_modes_bit_identical(corpus, mask, range_passages):
+    """Stage 3's walk-once kernel (mode 0, with the per-token kernel on ranges too dense for it)
+    and the per-token kernel alone (mode 1) give the same candidates, sums and counts."""
+    d, Q, E, oix, wix = corpus
+    ntok = _ntok(Q.shape[0]).cuda()
+    from ragrt_b200.weft import centroid_topk
+    topc, sc, _, _ = centroid_topk(Q.cuda(), d["centroids"].cuda(), 32, impute=True, ntok=ntok)
+    masks = torch.full((Q.shape[0],), mask, dtype=torch.int32, device="cuda")
+    out = []
+    for mode in (0, 1):
+        wix.set_stage3_mode(mode, range_passages)
+        wix.stats(reset=True)
+        out.append(wix.candidates(topc, sc, 700, ntok=ntok, masks=masks) + (wix.stats(),))
+    wix.set_stage3_mode(0)
+    (p0, s0, t0, st0), (p1, s1, t1, st1) = out
+    assert torch.equal(p0, p1) and torch.equal(s0, s1) and torch.equal(t0, t1)
+    for k in ("postings", "distinct_postings", "touched", "probes", "tasks"):
+        assert st0[k] == st1[k], k
+
+
 def test_stage3_full_scores_and_eid_limit(corpus):
     d, Q, E, oix, wix = corpus
     ntok = _ntok(Q.shape[0])
