@@ -196,26 +196,18 @@ def test_stage4_matches_fp32_reference():
     assert np.abs(out[fin] - ref[fin]).max() <= 1e-4 * np.abs(ref[fin]).max()
 
 
-def test_plain_ivf_and_packing_golden():
-    from ragrt_b200.compat import build_plain_ivf as B, ragrt_index_lib as L
+def test_pid_packing_golden():
+    """24-bit little-endian pid packing and unpacking against the reference library's own
+    output on its edge pids (0, 255, 256, 2^16, 2^24 - 1, ...), and out-of-range rejection."""
+    import torch
+    from ragrt_b200 import index_build
     g = _load("plain_ivf")
-    codes, dl = g["codes"], g["doclens"]
-    pids = np.repeat(np.arange(len(dl)), dl)
-    for ml in (65535, 5):
-        r = B.plain_ivf_csr(codes, pids, int(g["num_centroids"]), max_len=ml)
-        for k in ("row_ptrs", "col_eids", "lengths", "pids_sorted"):
-            assert np.array_equal(r[k], g[f"{k}_{ml}"]), (k, ml)
-        assert r["E_needed"] == int(g[f"E_needed_{ml}"])
-        lens16 = r["lengths"].astype(np.uint16)
-        assert np.array_equal(L.block_sums(lens16), g[f"block_sums_{ml}"])
-        assert np.array_equal(L.pack_pids_24(r["pids_sorted"]), g[f"packed_{ml}"])
-        assert np.array_equal(L.offsets_from_block_sums(L.block_sums(lens16), lens16, np.arange(len(lens16))),
-                              np.concatenate([[0], np.cumsum(r["lengths"])[:-1]]))
-    assert np.array_equal(L.pack_pids_24(g["edge_pids"]), g["edge_packed"])
-    assert np.array_equal(L.unpack_pids_24(g["edge_packed"]), g["edge_pids"])
-    for bad in ([L.MAX_PID + 1], [-1]):
+    edge = torch.from_numpy(np.asarray(g["edge_pids"], np.int64))
+    assert np.array_equal(index_build.pack_pids_24(edge).numpy(), g["edge_packed"])
+    assert np.array_equal(index_build.unpack_pids_24(torch.from_numpy(g["edge_packed"])).numpy(), g["edge_pids"])
+    for bad in ([(1 << 24)], [-1]):
         with pytest.raises(OverflowError):
-            L.pack_pids_24(np.array(bad))
+            index_build.pack_pids_24(torch.tensor(bad))
 
 
 def test_torch_index_builder_matches_reference_golden():
