@@ -150,6 +150,21 @@ int ragrt_weft_candidates(ragrt_index* index, const int32_t* d_topc, const float
 int ragrt_centroid_pass_counts(ragrt_index* index, uint32_t mask, int64_t* d_pass, int64_t* d_total, void* stream);
 
 /*
+ * Per-token probe depth under a filter: the rule of the reference's adaptive probing
+ * (src/weft_prep.py:75-106, engine weft_adapt).  d_topc [ntok, width] int32 holds each token's
+ * probed centroids best first; d_pass_c / d_tot_c [NC] int64 the passing / all postings per
+ * centroid (ragrt_centroid_pass_counts); sel the filter's global pass rate.  For each token,
+ * with target = sel x (all postings of its first nc probes), computed in fp32:
+ *   d_short[t] = 1 if its first nc probes hold fewer than slack x target passing postings;
+ *   d_need[t]  = 1 + the number of prefixes of its first ncap probes whose passing postings
+ *                are below the target, clamped to [nc, ncap].
+ * Needs 1 <= nc <= ncap <= width.
+ */
+int ragrt_probe_depth(const int32_t* d_topc, int32_t ntok, int32_t width, const int64_t* d_pass_c,
+                      const int64_t* d_tot_c, int32_t NC, float sel, float slack, int32_t nc, int32_t ncap,
+                      int32_t* d_short, int32_t* d_need, void* stream);
+
+/*
  * Stage 4: fused 2-bit residual decompression + TileMaxSim for B queries with n
  * candidates each.  Replaces launch_tile_maxsim_fused_decomp / native_tile_maxsim_fused_decomp
  * (tile_maxsim_fused_decomp.cu:125-251, optix_corr_torch_3d.cpp:865-883).

@@ -43,6 +43,7 @@ _SIGS = {
     "ragrt_centroid_topk_noalloc_error": (I32, [I32]),
     "ragrt_weft_candidates": (I32, [P, P, P, I32, P, I32, I32, I32, I32, P, I32, P, P, P, P]),
     "ragrt_centroid_pass_counts": (I32, [P, C.c_uint32, P, P, P]),
+    "ragrt_probe_depth": (I32, [P, I32, I32, P, P, I32, C.c_float, C.c_float, I32, I32, P, P, P]),
     "ragrt_tile_maxsim": (I32, [P, P, I32, I32, P, P, I32, P, P, P, P, P, P, P, I32, P]),
     "ragrt_tile_maxsim_exact": (I32, [P, P, I32, I32, P, P, I32, P, P, P]),
     "ragrt_final_topk": (I32, [P, P, I32, I32, P, I32, P, I32, P, P, P]),

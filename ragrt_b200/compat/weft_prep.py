@@ -66,64 +66,84 @@ def centroid_filter_counts(index, mask):
     return pass_c, tot_c, empty, int((~empty).sum())
 
 
-def _topk_values(Q, C, k):
-    """(vals float32 [ntok, k], idx int64 [ntok, k]): the k best fp16 scores (exact, ties to
-    the lower id), unshifted."""
-    topc, vals, _ = native_prep(Q, C, k, impute=False, compact=True)
-    return vals, topc.long()
+def _ranked(Q, C, k):
+    """Each token's k best centroids, best first (ties to the lower id), and their fp16 scores
+    as fp32, unshifted: (ids int32 [ntok, k], scores f32 [ntok, k])."""
+    ids, sc, _ = native_prep(Q, C, k, impute=False, compact=True)
+    return ids, sc
 
 
 def compact_centroids(C, empty):
-    """(C_ok [n_ok, d], ids int64 [n_ok]) -- the non-empty centroids (weft_prep.py:128-133);
-    C itself and None when no centroid is empty."""
-    if not bool(empty.any()):
+    """The centroids a filter leaves non-empty, once per filter (weft_prep.py:128-133):
+    (C_ok [n_ok, d], their ids int64 [n_ok]); when none is empty, C itself and None."""
+    keep = torch.nonzero(~empty).flatten()
+    if keep.numel() == C.shape[0]:
         return C, None
-    ids = (~empty).nonzero().squeeze(1)
-    return C[ids].contiguous(), ids
+    return C.index_select(0, keep).contiguous(), keep
 
 
 def oracle_fast_prep(Q, C_ok, ids, nc):
-    """Probe the nc nearest non-empty centroids, impute from the (nc+1)-th (weft_prep.py:136-144).
-    Returns (topc int32 [ntok, nc'], compact shifted scores, raw score of the last probed)."""
-    nc = min(nc, C_ok.shape[0] - 1)
-    topc, scores, m = native_prep(Q, C_ok, nc, impute=True, compact=True)
+    """weft_oracle's probes (weft_prep.py:136-144): each token's nc nearest non-empty centroids,
+    scores shifted by the (nc+1)-th.  Returns (topc int32 [ntok, nc'] as ids of the full centroid
+    set, shifted scores f32 [ntok, nc'], raw score of each token's last probed centroid)."""
+    depth = min(nc, C_ok.shape[0] - 1)
+    probes, raw = _ranked(Q, C_ok, depth + 1)
+    shifted = raw[:, :depth] - raw[:, depth:depth + 1]
     if ids is not None:
-        topc = ids[topc.long()].to(torch.int32).contiguous()
-    return topc, scores, scores[:, -1] + m
+        probes = ids.index_select(0, probes.reshape(-1).long()).view(probes.shape).to(torch.int32)
+    return probes[:, :depth].contiguous(), shifted.contiguous(), raw[:, depth - 1]
 
 
 def oracle_prep(Q, C, nc, empty, n_ok):
-    """Reference form of oracle_fast_prep (weft_prep.py:112-125); also returns depth = mean over
-    tokens of how many centroids (empty or not) score >= the last probed one."""
+    """weft_oracle's probes with its diagnostic depth (weft_prep.py:112-125): also returns the
+    mean over tokens of how many centroids, empty or not, score at least the last probed one."""
     C_ok, ids = compact_centroids(C, empty)
     topc, scores, last = oracle_fast_prep(Q, C_ok, ids, min(nc, n_ok - 1))
     return topc, scores, unfiltered_depth(Q, C, last)
 
 
 def unfiltered_depth(Q, C, last):
-    """Mean over tokens of the number of centroids scoring >= `last` (weft_prep.py:147-149)."""
+    """Mean over tokens of the number of centroids scoring >= `last` (weft_prep.py:147-149),
+    from the fp16 score matrix of the Stage-2 kernel."""
     _, full, _ = native_prep(Q, C, 1, impute=False, compact=False)
     return (full >= last.float()[:, None]).sum(1).float().mean()
 
 
+def _depths(probes, pass_c, tot_c, sel, nc, ncap, slack):
+    """ragrt_probe_depth on a token x probe list: (short int32 [ntok], need int32 [ntok])."""
+    from ragrt_b200._lib import lib, check
+    from ragrt_b200.weft import _ptr, _stream
+    probes = probes.to(torch.int32).contiguous()
+    ntok, width = probes.shape
+    pc = pass_c.to(device=probes.device, dtype=torch.int64).contiguous()
+    tc = tot_c.to(device=probes.device, dtype=torch.int64).contiguous()
+    short = torch.empty(ntok, dtype=torch.int32, device=probes.device)
+    need = torch.empty(ntok, dtype=torch.int32, device=probes.device)
+    check(lib().ragrt_probe_depth(_ptr(probes), ntok, width, _ptr(pc), _ptr(tc), pc.shape[0], float(sel),
+                                  float(slack), nc, ncap, _ptr(short), _ptr(need), _stream()))
+    return short, need
+
+
 def adaptive_probe(Q, C, nc, ncap, pass_c, tot_c, sel, q=1.0, slack=1.0, stats=None):
-    """weft_adapt's probe depth under a filter (weft_prep.py:75-105), same arguments and result
-    (topc int32 [ntok, nc'], compact shifted scores, nc')."""
+    """weft_adapt's probe depth under a filter (weft_prep.py:75-105); same arguments and result:
+    (topc int32 [ntok, d], compact scores shifted by the (d+1)-th f32 [ntok, d], d).
+
+    The depth d is nc unless more than a (1 - q) share of the tokens is short (their first nc
+    probes hold fewer than slack x the target passing postings, ragrt_probe_depth); then every
+    token's need is measured on its first ncap probes and d is their q-quantile (q = 1: the
+    largest), within [nc, ncap]."""
     NC = C.shape[0]
-    nc = min(nc, NC - 1)
-    ncap = min(ncap, NC - 1)
-    vals, idx = _topk_values(Q, C, nc + 1)
-    target = sel * tot_c[idx[:, :nc]].sum(1)
-    short = (pass_c[idx[:, :nc]].sum(1) < slack * target).float().mean()
-    if float(short) <= 1.0 - q + 1e-9:
-        nc2 = nc
-    else:
-        vals, idx = _topk_values(Q, C, ncap + 1)
-        cum = pass_c[idx[:, :ncap]].cumsum(1)
-        need = ((cum < target[:, None]).sum(1) + 1).clamp(nc, ncap).float()
-        nc2 = int(torch.quantile(need, q).ceil()) if q < 1.0 else int(need.max())
-        nc2 = max(nc, min(ncap, nc2))
-    m = vals[:, nc2]
+    nc, ncap = min(nc, NC - 1), min(ncap, NC - 1)
+    probes, raw = _ranked(Q, C, nc + 1)
+    short, _ = _depths(probes, pass_c, tot_c, sel, nc, nc, slack)
+    depth = nc
+    if float(short.float().mean()) > 1.0 - q + 1e-9:
+        probes, raw = _ranked(Q, C, ncap + 1)
+        _, need = _depths(probes, pass_c, tot_c, sel, nc, ncap, slack)
+        need = need.float()
+        d = int(need.max()) if q >= 1.0 else int(torch.quantile(need, q).ceil())
+        depth = max(nc, min(ncap, d))
     if stats is not None:
-        stats["last"] = vals[:, nc2 - 1]
-    return idx[:, :nc2].to(torch.int32).contiguous(), (vals[:, :nc2] - m[:, None]).contiguous(), nc2
+        stats["last"] = raw[:, depth - 1]
+    shifted = raw[:, :depth] - raw[:, depth:depth + 1]
+    return probes[:, :depth].contiguous(), shifted.contiguous(), depth
