@@ -11,22 +11,26 @@
 // share topics: about 1,000 kept probes but 250 distinct lists on the benchmark corpus), so
 // walking per (token, probe) reads every list about four times.  Here:
 //
-//   s3_prep   (a CTA per query) sorts the kept (centroid, token, v) triples by centroid and
-//             writes the query's distinct lists, each with its (token, v) pairs; it also counts
-//             the diagnostic statistics (postings of every kept probe, distinct postings, kept
-//             probes, tasks).
-//   s3_walk   (persistent CTAs; a work item is one query and a block of pid ranges) splits each
-//             CTA into independent teams of warps.  A team walks one pid range at a time: each
-//             distinct list's sub-list in the range once, coalesced.  A touched passage gets a
-//             row of 32 per-token maxima (fp16 bits, 16-bit compare-and-swap maximum: positive
-//             fp16 values order like their bits) in the team's shared-memory hash table, keyed
-//             by pid; every posting applies its list's (token, v) pairs to that row.  At the
-//             end of the range each row's 32 maxima are summed exactly (fixed point, 2^-24
-//             units), rounded once to fp32 and emitted as a ranking key into the query's pool,
-//             as the per-token kernel does.  A range that touches more passages than the table
-//             holds is pushed to a queue and handled by the per-token kernel (s3_accumulate in
-//             queue mode), which needs no per-passage rows.  Teams synchronise on their own
-//             named barrier only, so a range's short phases do not hold up the whole CTA.
+//   s3_prep    (a CTA per query) sorts the kept (centroid, token, v) triples by centroid and
+//              writes the query's distinct lists, each with its row of 32 per-token values
+//              (fp16 bits, 0 for a token that did not probe the list); it also counts the
+//              diagnostic statistics (postings of every kept probe, distinct postings, kept
+//              probes, tasks).
+//   s3_bucket  (persistent CTAs; a work item is one query and a block of pid ranges) takes one
+//              pid range at a time and
+//                A. finds each distinct list's sub-list inside the range (the index's
+//                   range-offset table) and their prefix: the range's entries;
+//                B. walks the entries once, coalesced; an entry (passage, list) takes the next
+//                   slot of its passage (a 16-bit counter per passage, two per shared word), and
+//                   the entry that takes slot 0 records the passage as touched;
+//                C. scans the touched passages' counts into their offsets;
+//                D. files every entry's list under its passage (a counting sort);
+//                E. gives each touched passage four lanes, 8 tokens each, which max-reduce the
+//                   value rows of the passage's lists with 16-byte loads, then sum the 32
+//                   maxima exactly (fixed point, 2^-24 units), round once to fp32 and emit the
+//                   ranking key into the query's pool, as the per-token kernel does.
+//              A range whose entries exceed the staging area is pushed to a queue and handled
+//              by the per-token kernel (s3_accumulate in queue mode), which has no such limit.
 //
 // Both kernels produce bit-identical sums (the per-(passage, token) maximum is order-free and the
 // sum is exact), so the split between them never changes a result.
@@ -39,13 +43,14 @@
 namespace ragrt {
 
 constexpr int kPrepThreads = 512;
-constexpr int kTeamWarps = 4;            // warps of a team: one walk range at a time, own hash table
-constexpr int kWalkTeams = 2;
-constexpr int kWalkWarps = kWalkTeams * kTeamWarps;
-constexpr int kWalkThreads = kWalkWarps * 32;
-constexpr int kBatch = 2;                // 32-entry chunks whose pid loads a warp issues together
-constexpr int kUnit = 32 * kBatch;       // entries of one list group per work unit of a warp
-constexpr uint32_t kEmpty = 0xFFFFFFFFu;
+constexpr int kBkWarps = 8;
+constexpr int kBkThreads = kBkWarps * 32;
+constexpr int kBkMaxW = 4096;             // passages per pid range (12-bit local pids)
+constexpr int kBkMaxLists = 1024;         // distinct lists per query (10-bit list ids)
+constexpr int kBkStage = 3072;            // entries per range held in shared memory
+constexpr int kBatch = 2;                 // 32-entry chunks whose pid loads a warp issues together
+constexpr int kUnit = 32 * kBatch;        // entries of one list group per work unit of a warp
+constexpr uint32_t kNoEntry = 0xFFFFFFFFu;
 
 __device__ __forceinline__ uint16_t s3_v15(float base) {
     return (uint16_t)(__half_as_ushort(__float2half_rn(base)) & 0x7FFF);   // ragrt_fused_kernel.cu:366
@@ -93,12 +98,11 @@ struct S3PrepParams {
     const int64_t* rp;
     const int64_t* list_off;
     int n_eids;
-    int LM;                          // list / pair capacity per query (rows * kc)
+    int LM;                          // list capacity per query (rows * kc)
     int32_t* nl;                     // [nq]
     int32_t* lc;                     // [nq][LM] centroid of list j
     int32_t* lpc;                    // [nq][LM] postings of list j (its first n_eids chunk lists)
-    int32_t* lpo;                    // [nq][LM + 1] first pair of list j
-    uint32_t* pairs;                 // [nq][LM] (token << 16) | fp16 bits of v, grouped by list
+    uint16_t* val;                   // [nq][LM][32] value of token t for list j (fp16 bits; 0: not probed)
     unsigned long long* stats;
 };
 
@@ -127,44 +131,38 @@ s3_prep(S3PrepParams p) {
     }
     __syncthreads();
     cta_bitonic_sort<false>(pk, P);
-    // each thread owns a contiguous run of the sorted keys; list starts are where c changes
+    // each thread owns a contiguous run of the sorted keys; lists start where the centroid changes
     const int per = (P + blockDim.x - 1) / blockDim.x;
     const int i0 = threadIdx.x * per, i1 = min(P, i0 + per);
     int starts = 0;
     for (int i = i0; i < i1; ++i)
         if (pk[i] != ~0ull && (i == 0 || (pk[i] >> 32) != (pk[i - 1] >> 32))) ++starts;
     int nlists = 0;
-    int j = cta_excl_scan(starts, s_scan, &nlists);
-    unsigned long long st_post = 0, st_dist = 0, st_tasks = 0, st_probes = 0;
+    const int j0 = cta_excl_scan(starts, s_scan, &nlists);
     int32_t* lc = p.lc + (int64_t)qi * p.LM;
     int32_t* lpc = p.lpc + (int64_t)qi * p.LM;
-    int32_t* lpo = p.lpo + (int64_t)qi * (p.LM + 1);
-    uint32_t* pairs = p.pairs + (int64_t)qi * p.LM;
-    int last = -1;
+    uint16_t* val = p.val + (int64_t)qi * p.LM * 32;
+    for (int i = threadIdx.x; i < nlists * 16; i += blockDim.x) reinterpret_cast<uint32_t*>(val)[i] = 0u;
+    __syncthreads();
+    unsigned long long st_post = 0, st_dist = 0, st_tasks = 0, st_probes = 0;
+    int j = j0 - 1;                       // list of the previous key (this run may start inside one)
     for (int i = i0; i < i1; ++i) {
         const uint64_t k = pk[i];
-        if (k == ~0ull) {
-            if (i == 0 || pk[i - 1] != ~0ull) lpo[nlists] = i;          // end of the last list
-            break;
-        }
+        if (k == ~0ull) break;
         const int c = (int)(k >> 32);
-        pairs[i] = (uint32_t)(k & 0xFFFFFFFFu);
         const int nle = min(p.clists[c], p.n_eids);
         const int64_t cnt = nle > 0 ? p.list_off[p.rp[c] + nle] - p.cstart[c] : 0;
+        if (i == 0 || (pk[i - 1] >> 32) != (uint64_t)(uint32_t)c) {
+            ++j;
+            lc[j] = c;
+            lpc[j] = (int32_t)cnt;
+            st_dist += (unsigned long long)cnt;
+        }
+        val[(int64_t)j * 32 + ((k >> 16) & 31)] = (uint16_t)(k & 0xFFFFu);
         ++st_probes;
         st_tasks += (unsigned long long)max(nle, 0);
         st_post += (unsigned long long)cnt;
-        if (i == 0 || (pk[i - 1] >> 32) != (uint64_t)(uint32_t)c) {
-            lc[j] = c;
-            lpc[j] = (int32_t)cnt;
-            lpo[j] = i;
-            ++j;
-            st_dist += (unsigned long long)cnt;
-        }
-        last = i;
     }
-    // a run of kept keys that fills P exactly has no sentinel after it
-    if (last == P - 1) lpo[nlists] = P;
     if (threadIdx.x == 0) p.nl[qi] = nlists;
     if (p.stats) {
         for (int o = 16; o; o >>= 1) {
@@ -182,122 +180,87 @@ s3_prep(S3PrepParams p) {
     }
 }
 
-// ------------------------------------------------------------------ the walk
-struct S3WalkParams {
+// ------------------------------------------------------------------ the bucketed walk
+struct S3BucketParams {
     const uint8_t* packed;
     const uint32_t* preds;
     const uint32_t* boff;
     const int64_t* cstart;
     int N, R, w_shift;
-    int m;                           // index ranges per walk range
-    int RP;                          // walk ranges: ceil(R / m)
     const int32_t* nl;
     const int32_t* lc;
     const int32_t* lpc;
-    const int32_t* lpo;
-    const uint32_t* pairs;
+    const uint16_t* val;
     int LM;
     const uint32_t* masks;
     int q0, nq;
-    int rpj;                         // walk ranges per work item
-    int rcap_log2;                   // hash rows per team: 1 << rcap_log2
+    int rpj;                         // pid ranges per work item
     uint64_t* pool;
     int64_t pool_cap;
     unsigned long long* pool_count;  // [nq]
     unsigned int* work;
-    unsigned long long* dense;       // deferred (qi << 32 | walk range)
+    unsigned long long* dense;       // deferred (qi << 32 | range)
     unsigned int* dense_count;
-    unsigned long long* stats;       // [7] += deferred range blocks
+    unsigned long long* stats;       // [7] += deferred ranges
 };
 
-// Shared memory: the work item's query (its distinct lists, read by both teams), then one
-// block per team: its hash rows (32 per-token maxima as fp16 bits; token t of row h at column
-// t ^ (h & 31)), the rows' keys (pid - range_lo, or kEmpty) and its list groups' entry counts.
 __host__ __device__ inline size_t align128(size_t x) { return (x + 127) & ~(size_t)127; }
-__host__ __device__ inline size_t walk_query_bytes(int LM) {
-    return align128(sizeof(int64_t) * LM + 3 * sizeof(int32_t) * LM + sizeof(int32_t) * (LM + 1));
-}
-__host__ __device__ inline size_t walk_team_bytes(int LM, int rcap) {
-    return align128(sizeof(uint16_t) * (size_t)rcap * 32 + sizeof(uint32_t) * rcap + sizeof(int32_t) * (LM / 32 + 2));
-}
-__host__ __device__ inline size_t walk_smem_bytes(int LM, int rcap) {
-    return walk_query_bytes(LM) + kWalkTeams * walk_team_bytes(LM, rcap);
+// shared memory: counters [W/2] u32 | staging [kBkStage] u32 | filed lists [kBkStage] u16 |
+// touched passages [W] u16 | their first slot [W] u16 | per list: first posting in the range
+// [LM] i64, cstart [LM] i64, centroid [LM] i32, postings [LM] i32, entry prefix [LM + 1] i32
+__host__ __device__ inline size_t bucket_smem_bytes(int LM) {
+    return align128(4 * (kBkMaxW / 2)) + align128(4 * kBkStage) + align128(2 * kBkStage) + 2 * align128(2 * kBkMaxW) +
+           2 * align128(8 * (size_t)LM) + 2 * align128(4 * (size_t)LM) + align128(4 * (size_t)(LM + 1));
 }
 
-__device__ __forceinline__ void team_sync(int team) {
-    asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(kTeamWarps * 32) : "memory");
-}
-
-// per-token maximum of positive fp16 bits in a 16-bit slot (fp16 order = bit order for v >= 0)
-__device__ __forceinline__ void max16(uint16_t* a, uint16_t v) {
-    unsigned short old = *(volatile unsigned short*)a;
-    while (v > old) {
-        const unsigned short prev = atomicCAS(reinterpret_cast<unsigned short*>(a), old, (unsigned short)v);
-        if (prev == old) break;
-        old = prev;
-    }
-}
-
-__global__ void __launch_bounds__(kWalkThreads, 2)
-s3_walk(S3WalkParams p) {
-    extern __shared__ __align__(16) unsigned char walk_smem[];
-    const int rcap = 1 << p.rcap_log2;
+__global__ void __launch_bounds__(kBkThreads, 3)
+s3_bucket(S3BucketParams p) {
+    extern __shared__ __align__(128) unsigned char bk_smem[];
     const int LM = p.LM;
-    int64_t* lcs = reinterpret_cast<int64_t*>(walk_smem);                 // [LM] cstart of list j
-    int32_t* lcx = reinterpret_cast<int32_t*>(lcs + LM);                  // [LM] centroid
-    int32_t* lpcx = lcx + LM;                                              // [LM] postings
-    uint32_t* pairsx = reinterpret_cast<uint32_t*>(lpcx + LM);            // [LM]
-    int32_t* lpox = reinterpret_cast<int32_t*>(pairsx + LM);              // [LM + 1]
+    unsigned char* sp = bk_smem;
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(sp);    sp += align128(4 * (kBkMaxW / 2));
+    uint32_t* stg = reinterpret_cast<uint32_t*>(sp);    sp += align128(4 * kBkStage);
+    uint16_t* srt = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkStage);
+    uint16_t* tpp = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkMaxW);
+    uint16_t* tpo = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkMaxW);
+    int64_t* segs = reinterpret_cast<int64_t*>(sp);     sp += align128(8 * (size_t)LM);
+    int64_t* lcs = reinterpret_cast<int64_t*>(sp);      sp += align128(8 * (size_t)LM);
+    int32_t* lcx = reinterpret_cast<int32_t*>(sp);      sp += align128(4 * (size_t)LM);
+    int32_t* lpcx = reinterpret_cast<int32_t*>(sp);     sp += align128(4 * (size_t)LM);
+    int32_t* segpre = reinterpret_cast<int32_t*>(sp);
+    __shared__ int s_scan[33];
+    __shared__ unsigned s_job;
+    __shared__ int s_nl, s_valid;
+    __shared__ unsigned s_touched;
+    __shared__ unsigned long long s_base;
+
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-    const int team = w / kTeamWarps, tw = w % kTeamWarps, tt = tid % (kTeamWarps * 32);
-    unsigned char* tbase = walk_smem + walk_query_bytes(LM) + (size_t)team * walk_team_bytes(LM, rcap);
-    uint16_t* rows = reinterpret_cast<uint16_t*>(tbase);                  // [rcap][32]
-    uint32_t* keys = reinterpret_cast<uint32_t*>(rows + (size_t)rcap * 32);
-    int32_t* gtot = reinterpret_cast<int32_t*>(keys + rcap);              // [LM / 32 + 1]
-
-    __shared__ unsigned s_job, s_rctr;
-    __shared__ int s_nl;
-    __shared__ int s_trange[kWalkTeams];
-    __shared__ unsigned s_nkeys[kWalkTeams];
-    __shared__ int s_overflow[kWalkTeams];
-    __shared__ unsigned s_wcnt[kWalkTeams][kTeamWarps];
-    __shared__ unsigned long long s_base[kWalkTeams];
-    __shared__ uint32_t s_slots[kWalkWarps][32];      // emission: the warp's occupied slots in order
-
-    for (int i = tt; i < rcap * 16; i += kTeamWarps * 32) reinterpret_cast<uint32_t*>(rows)[i] = 0u;
-    for (int i = tt; i < rcap; i += kTeamWarps * 32) keys[i] = kEmpty;
-    if (tt == 0) { s_nkeys[team] = 0; s_overflow[team] = 0; }
-    const unsigned nrb = ((unsigned)p.RP + p.rpj - 1) / p.rpj;
+    const int W = 1 << p.w_shift;
+    uint16_t* cnt16 = reinterpret_cast<uint16_t*>(cnt);
+    for (int i = tid; i < (W >> 1); i += kBkThreads) cnt[i] = 0u;
+    if (tid == 0) s_touched = 0;
+    const unsigned nrb = ((unsigned)p.R + p.rpj - 1) / p.rpj;
     const unsigned total_jobs = (unsigned)p.nq * nrb;
-    const unsigned max_keys = (unsigned)(rcap - (rcap >> 2) - (rcap >> 3));   // 5/8 load
     int cached_q = -1;
     __syncthreads();
 
     for (;;) {
-        if (tid == 0) {
-            s_job = atomicAdd(p.work, 1u);
-            s_rctr = 0;
-        }
+        if (tid == 0) s_job = atomicAdd(p.work, 1u);
         __syncthreads();
         const unsigned job = s_job;
         if (job >= total_jobs) break;
         const int qi = (int)(job / nrb);
-        const int rp0 = (int)(job % nrb) * p.rpj, rp1 = min(p.RP, rp0 + p.rpj);
+        const int r0 = (int)(job % nrb) * p.rpj, r1 = min(p.R, r0 + p.rpj);
         if (qi != cached_q) {
             const int nl = p.nl[qi];
             const int32_t* lc = p.lc + (int64_t)qi * LM;
             const int32_t* lpc = p.lpc + (int64_t)qi * LM;
-            const int32_t* lpo = p.lpo + (int64_t)qi * (LM + 1);
-            for (int j = tid; j < nl; j += kWalkThreads) {
+            for (int j = tid; j < nl; j += kBkThreads) {
                 const int c = lc[j];
                 lcx[j] = c;
                 lpcx[j] = lpc[j];
                 lcs[j] = p.cstart[c];
             }
-            for (int j = tid; j <= nl; j += kWalkThreads) lpox[j] = lpo[j];
-            const int np = nl ? lpo[nl] : 0;
-            const uint32_t* pr = p.pairs + (int64_t)qi * LM;
-            for (int k = tid; k < np; k += kWalkThreads) pairsx[k] = pr[k];
             if (tid == 0) s_nl = nl;
             cached_q = qi;
             __syncthreads();
@@ -305,216 +268,193 @@ s3_walk(S3WalkParams p) {
         const int nl = s_nl;
         const int ngroups = (nl + 31) >> 5;
         const uint32_t mask = p.masks ? p.masks[p.q0 + qi] : 0u;
+        const uint4* qval = reinterpret_cast<const uint4*>(p.val + (int64_t)qi * LM * 32);
 
-        // the teams take the work item's walk ranges one at a time
-        for (;;) {
-            if (tt == 0) s_trange[team] = rp0 + (int)atomicAdd(&s_rctr, 1u);
-            team_sync(team);
-            const int rpi = s_trange[team];
-            if (rpi >= rp1) break;                                            // team-uniform
-            const int r = rpi * p.m, rend = min(p.R, r + p.m);
+        for (int r = r0; r < r1; ++r) {
             const int64_t range_lo = (int64_t)r << p.w_shift;
-            const int64_t range_w = ((int64_t)(rend - r)) << p.w_shift;
 
-            // ---- 1. entries per group of 32 lists: the lists' sub-lists inside the range
-            for (int g = tw; g < ngroups; g += kTeamWarps) {
-                const int j = 32 * g + lane;
-                int len = 0;
-                if (j < nl) {
-                    const uint32_t* bo = p.boff + (int64_t)lcx[j] * (p.R + 1);
-                    const int64_t hi = min((int64_t)bo[rend], (int64_t)lpcx[j]);
-                    len = (int)(hi - min((int64_t)bo[r], hi));
-                }
-#pragma unroll
-                for (int o = 16; o; o >>= 1) len += __shfl_xor_sync(0xFFFFFFFFu, len, o);
-                if (lane == 0) gtot[g] = len;
+            // ---- A. each list's sub-list inside the range; entry prefix over the lists
+            const int per = (nl + kBkThreads - 1) / kBkThreads;
+            const int ja = tid * per, jb = min(nl, ja + per);
+            int mylen = 0;
+            for (int j = ja; j < jb; ++j) {
+                const uint32_t* bo = p.boff + (int64_t)lcx[j] * (p.R + 1);
+                const int64_t hi = min((int64_t)bo[r + 1], (int64_t)lpcx[j]);
+                const int64_t lo = min((int64_t)bo[r], hi);
+                segs[j] = lcs[j] + lo;
+                segpre[j] = (int)(hi - lo);                  // length for now
+                mylen += (int)(hi - lo);
             }
-            team_sync(team);
-
-            // ---- 2. walk: the team's warps take units of kUnit consecutive entries of a group
-            int ubase = 0;
-            for (int g = 0; g < ngroups; ++g) {
-                const int tg = gtot[g];
-                const int ug = (tg + kUnit - 1) / kUnit;
-                const int k0 = ((tw - ubase) % kTeamWarps + kTeamWarps) % kTeamWarps;
-                ubase += ug;
-                if (k0 >= ug) continue;                                       // warp-uniform
-                // this warp's view of the group: lane = list, its sub-list and exclusive prefix
-                const int j = 32 * g + lane;
-                int len = 0;
-                int64_t start = 0;
-                if (j < nl) {
-                    const uint32_t* bo = p.boff + (int64_t)lcx[j] * (p.R + 1);
-                    const int64_t hi = min((int64_t)bo[rend], (int64_t)lpcx[j]);
-                    const int64_t lo = min((int64_t)bo[r], hi);
-                    len = (int)(hi - lo);
-                    start = lcs[j] + lo;
-                }
-                int incl = len;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-                    if (lane >= o) incl += y;
-                }
-                const int excl = j < nl ? incl - len : tg;                    // past the lists: never chosen
-                const int64_t sbase = start - excl;                           // posting of entry e: sbase + e
-                for (int k = k0; k < ug; k += kTeamWarps) {
-                    const int e_beg = k * kUnit, e_end = min(tg, e_beg + kUnit);
-                    int32_t pid[kBatch];
-                    int src[kBatch];
-#pragma unroll
-                    for (int b = 0; b < kBatch; ++b) {
-                        const int e = e_beg + 32 * b + lane;
-                        int s = 0;
-#pragma unroll
-                        for (int step = 16; step; step >>= 1) {
-                            const int cand = s + step;
-                            const int ex = __shfl_sync(0xFFFFFFFFu, excl, cand & 31);
-                            if (cand < 32 && ex <= e) s = cand;
-                        }
-                        const int64_t sb = __shfl_sync(0xFFFFFFFFu, sbase, s);
-                        src[b] = 32 * g + s;
-                        pid[b] = e < e_end ? load_pid24(p.packed, sb + e) : -1;
-                    }
-                    if (mask) {
-#pragma unroll
-                        for (int b = 0; b < kBatch; ++b)
-                            if (pid[b] >= 0 && pid[b] < p.N && !(p.preds[pid[b]] & mask)) pid[b] = -1;  // :387
-                    }
-#pragma unroll
-                    for (int b = 0; b < kBatch; ++b) {
-                        if (e_beg + 32 * b >= e_end) break;                   // warp-uniform
-                        const int64_t pl64 = (int64_t)pid[b] - range_lo;
-                        const bool ok = pid[b] >= 0 && pl64 >= 0 && pl64 < range_w &&
-                                        !*(volatile int*)&s_overflow[team];
-                        int row = -1;
-                        bool fresh = false;
-                        if (ok) {
-                            const uint32_t pl = (uint32_t)pl64;
-                            uint32_t h = (pl * 0x9E3779B1u) >> (32 - p.rcap_log2);
-                            for (int probe = 0; probe < rcap; ++probe) {
-                                const uint32_t old = atomicCAS(&keys[h], kEmpty, pl);
-                                if (old == kEmpty || old == pl) {
-                                    row = (int)h;
-                                    fresh = old == kEmpty;
-                                    break;
-                                }
-                                h = (h + 1) & (uint32_t)(rcap - 1);
-                            }
-                            if (row < 0) s_overflow[team] = 1;
-                        }
-                        const unsigned nf = __ballot_sync(0xFFFFFFFFu, fresh);
-                        if (nf && lane == 0) {
-                            const unsigned before = atomicAdd(&s_nkeys[team], (unsigned)__popc(nf));
-                            if (before + __popc(nf) > max_keys) s_overflow[team] = 1;
-                        }
-                        if (row >= 0) {
-                            const int js = src[b];
-                            const int a0 = lpox[js], a1 = lpox[js + 1];
-                            uint16_t* rw = rows + (size_t)row * 32;
-                            const int sw = row & 31;
-                            for (int a = a0; a < a1; ++a) {
-                                const uint32_t tv = pairsx[a];
-                                max16(rw + ((tv >> 16) ^ sw), (uint16_t)(tv & 0xFFFFu));
-                            }
-                        }
-                    }
-                }
+            int total = 0;
+            int run = cta_excl_scan(mylen, s_scan, &total);
+            for (int j = ja; j < jb; ++j) {
+                const int len = segpre[j];
+                segpre[j] = run;
+                run += len;
             }
-            team_sync(team);
-
-            // ---- 3. emit every touched passage's exact sum, or defer the range
-            const int per_w = rcap / kTeamWarps;
-            if (s_overflow[team]) {
-                for (int i = tt; i < rcap; i += kTeamWarps * 32) {
-                    if (keys[i] != kEmpty) {
-                        uint4* rr = reinterpret_cast<uint4*>(rows + (size_t)i * 32);
-#pragma unroll
-                        for (int x = 0; x < 4; ++x) rr[x] = make_uint4(0u, 0u, 0u, 0u);
-                        keys[i] = kEmpty;
-                    }
-                }
-                if (tt == 0) {
+            if (tid == 0) segpre[nl] = total;
+            __syncthreads();
+            if (total > kBkStage) {                          // too many entries: the per-token kernel
+                if (tid == 0) {
                     const unsigned pos = atomicAdd(p.dense_count, 1u);
-                    p.dense[pos] = ((unsigned long long)qi << 32) | (unsigned)rpi;
+                    p.dense[pos] = ((unsigned long long)qi << 32) | (unsigned)r;
                     if (p.stats) atomicAdd(&p.stats[7], 1ull);
                 }
-            } else {
-                unsigned cnt = 0;
-                for (int i0 = 0; i0 < per_w; i0 += 32)
-                    cnt += __popc(__ballot_sync(0xFFFFFFFFu,
-                                                i0 + lane < per_w && keys[tw * per_w + i0 + lane] != kEmpty));
-                if (lane == 0) s_wcnt[team][tw] = cnt;
-                team_sync(team);
-                if (tt == 0) {
-                    unsigned t = 0;
-                    for (int i = 0; i < kTeamWarps; ++i) { const unsigned c = s_wcnt[team][i]; s_wcnt[team][i] = t; t += c; }
-                    s_base[team] = t ? atomicAdd(&p.pool_count[qi], (unsigned long long)t) : 0ull;
-                }
-                team_sync(team);
-                uint64_t* pool = p.pool + (int64_t)qi * p.pool_cap + s_base[team] + s_wcnt[team][tw];
-                unsigned done = 0;
-                for (int i0 = 0; i0 < per_w; i0 += 32) {
-                    const int slot = tw * per_w + i0 + lane;
-                    const bool occ = i0 + lane < per_w && keys[slot] != kEmpty;
-                    const unsigned mk = __ballot_sync(0xFFFFFFFFu, occ);
-                    if (occ) s_slots[w][__popc(mk & ((1u << lane) - 1u))] = (uint32_t)slot;
-                    __syncwarp();
-                    const int n = __popc(mk);
-                    for (int r0 = 0; r0 < n; r0 += 8) {                     // 4 lanes per row
-                        const int ri = r0 + (lane >> 2), qd = lane & 3;
-                        unsigned long long sum = 0;
-                        int sl = 0;
-                        if (ri < n) {
-                            sl = (int)s_slots[w][ri];
-                            uint4* rr = reinterpret_cast<uint4*>(rows + (size_t)sl * 32 + qd * 8);
-                            const uint4 a = rr[0];
-                            sum = h_fixed24((uint16_t)a.x) + h_fixed24((uint16_t)(a.x >> 16)) +
-                                  h_fixed24((uint16_t)a.y) + h_fixed24((uint16_t)(a.y >> 16)) +
-                                  h_fixed24((uint16_t)a.z) + h_fixed24((uint16_t)(a.z >> 16)) +
-                                  h_fixed24((uint16_t)a.w) + h_fixed24((uint16_t)(a.w >> 16));
-                            rr[0] = make_uint4(0u, 0u, 0u, 0u);
+                __syncthreads();
+                continue;
+            }
+            if (total == 0) continue;                        // CTA-uniform
+
+            // ---- B. walk: units of kUnit entries of one group of 32 lists, warps round robin
+            {
+                int ubase = 0;
+                for (int g = 0; g < ngroups; ++g) {
+                    const int gb = segpre[32 * g];
+                    const int tg = segpre[min(nl, 32 * g + 32)] - gb;
+                    const int ug = (tg + kUnit - 1) / kUnit;
+                    const int k0 = ((w - ubase) % kBkWarps + kBkWarps) % kBkWarps;
+                    ubase += ug;
+                    if (k0 >= ug) continue;                  // warp-uniform
+                    const int jl = 32 * g + lane;
+                    const int excl = (jl < nl ? segpre[jl] : segpre[nl]) - gb;
+                    const int64_t sbase = (jl < nl ? segs[jl] : 0) - excl;    // posting of entry e: sbase + e
+                    for (int k = k0; k < ug; k += kBkWarps) {
+                        const int e_beg = k * kUnit, e_end = min(tg, e_beg + kUnit);
+                        int32_t pid[kBatch];
+                        int src[kBatch];
+#pragma unroll
+                        for (int b = 0; b < kBatch; ++b) {
+                            const int e = e_beg + 32 * b + lane;
+                            int s = 0;
+#pragma unroll
+                            for (int step = 16; step; step >>= 1) {
+                                const int cand = s + step;
+                                const int ex = __shfl_sync(0xFFFFFFFFu, excl, cand & 31);
+                                if (cand < 32 && ex <= e) s = cand;
+                            }
+                            const int64_t sb = __shfl_sync(0xFFFFFFFFu, sbase, s);
+                            src[b] = 32 * g + s;
+                            pid[b] = e < e_end ? load_pid24(p.packed, sb + e) : -1;
                         }
-                        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-                        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
-                        if (ri < n && qd == 0) {
-                            const float sc = __ull2float_rn(sum) * 0x1p-24f;
-                            pool[done + ri] = rank_key(sc, (int32_t)(range_lo + keys[sl]));
-                            keys[sl] = kEmpty;
+                        if (mask) {
+#pragma unroll
+                            for (int b = 0; b < kBatch; ++b)
+                                if (pid[b] >= 0 && pid[b] < p.N && !(p.preds[pid[b]] & mask)) pid[b] = -2;  // :387
+                        }
+#pragma unroll
+                        for (int b = 0; b < kBatch; ++b) {
+                            const int e = e_beg + 32 * b + lane;
+                            const int64_t pl = (int64_t)pid[b] - range_lo;
+                            uint32_t word = kNoEntry;
+                            bool first = false;
+                            if (e < e_end && pid[b] >= 0 && pl >= 0 && pl < W) {
+                                const int sh = 16 * ((int)pl & 1);
+                                const uint32_t old = atomicAdd(&cnt[pl >> 1], 1u << sh);
+                                const uint32_t slot = (old >> sh) & 0xFFFFu;
+                                word = (uint32_t)pl | ((uint32_t)src[b] << 12) | (slot << 22);
+                                first = slot == 0;
+                            }
+                            // the passages this chunk touches first: one reservation per warp
+                            const unsigned fm = __ballot_sync(0xFFFFFFFFu, first);
+                            unsigned tb = 0;
+                            if (fm && lane == 0) tb = atomicAdd(&s_touched, (unsigned)__popc(fm));
+                            tb = __shfl_sync(0xFFFFFFFFu, tb, 0);
+                            if (first) tpp[tb + __popc(fm & ((1u << lane) - 1u))] = (uint16_t)pl;
+                            if (e < e_end) stg[gb + e] = word;
                         }
                     }
-                    done += n;
-                    __syncwarp();
                 }
             }
-            if (tt == 0) { s_nkeys[team] = 0; s_overflow[team] = 0; }
-            team_sync(team);
+            __syncthreads();
+
+            // ---- C. offsets of the touched passages' entries (written over their counters)
+            {
+                const int T = (int)s_touched;
+                const int per_t = (T + kBkThreads - 1) / kBkThreads;
+                const int ta = tid * per_t, tb = min(T, ta + per_t);
+                int mine = 0;
+                for (int i = ta; i < tb; ++i) mine += cnt16[tpp[i]];
+                int valid = 0;
+                int run = cta_excl_scan(mine, s_scan, &valid);
+                for (int i = ta; i < tb; ++i) {
+                    const int pl = tpp[i];
+                    const int c = cnt16[pl];
+                    tpo[i] = (uint16_t)run;
+                    cnt16[pl] = (uint16_t)run;
+                    run += c;
+                }
+                if (tid == 0) {
+                    s_valid = valid;
+                    s_base = T ? atomicAdd(&p.pool_count[qi], (unsigned long long)T) : 0ull;
+                }
+            }
+            __syncthreads();
+
+            // ---- D. file every entry's list under its passage
+            for (int e = tid; e < total; e += kBkThreads) {
+                const uint32_t word = stg[e];
+                if (word == kNoEntry) continue;
+                const int pl = (int)(word & 0xFFFu);
+                const uint32_t off = (cnt[pl >> 1] >> (16 * (pl & 1))) & 0xFFFFu;
+                srt[off + (word >> 22)] = (uint16_t)((word >> 12) & 0x3FFu);
+            }
+            __syncthreads();
+
+            // ---- E. per touched passage: max over its lists' value rows, exact sum, ranking key
+            {
+                const int T = (int)s_touched, V = s_valid;
+                uint64_t* pool = p.pool + (int64_t)qi * p.pool_cap + s_base;
+                const int qd = lane & 3;
+                for (int t0 = w * 8; t0 < T; t0 += kBkWarps * 8) {
+                    const int ti = t0 + (lane >> 2);
+                    unsigned long long sum = 0;
+                    if (ti < T) {
+                        const int a = tpo[ti], b = ti + 1 < T ? tpo[ti + 1] : V;
+                        uint4 acc = make_uint4(0u, 0u, 0u, 0u);      // fp16 bits >= 0: unsigned max
+                        for (int k = a; k < b; ++k) {
+                            const uint4 v = qval[(int)srt[k] * 4 + qd];              // 8 tokens, fp16 bits
+                            acc.x = __vmaxu2(acc.x, v.x);
+                            acc.y = __vmaxu2(acc.y, v.y);
+                            acc.z = __vmaxu2(acc.z, v.z);
+                            acc.w = __vmaxu2(acc.w, v.w);
+                        }
+                        sum = h_fixed24((uint16_t)acc.x) + h_fixed24((uint16_t)(acc.x >> 16)) +
+                              h_fixed24((uint16_t)acc.y) + h_fixed24((uint16_t)(acc.y >> 16)) +
+                              h_fixed24((uint16_t)acc.z) + h_fixed24((uint16_t)(acc.z >> 16)) +
+                              h_fixed24((uint16_t)acc.w) + h_fixed24((uint16_t)(acc.w >> 16));
+                    }
+                    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+                    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+                    if (ti < T && qd == 0) {
+                        const float sc = __ull2float_rn(sum) * 0x1p-24f;
+                        pool[ti] = rank_key(sc, (int32_t)(range_lo + tpp[ti]));
+                    }
+                }
+            }
+            // ---- F. the touched passages' counters back to zero for the next range
+            for (int i = tid; i < (int)s_touched; i += kBkThreads) cnt16[tpp[i]] = 0;
+            __syncthreads();
+            if (tid == 0) s_touched = 0;
         }
-        __syncthreads();                                                      // the item is done
     }
 }
 
-// every (query, range block) into the per-token kernel's queue (Stage-3 mode 1)
-__global__ void s3_queue_all(int nq, int RP, unsigned long long* dense, unsigned int* dense_count) {
+// every (query, range) into the per-token kernel's queue (Stage-3 mode 1, or no room for the walk)
+__global__ void s3_queue_all(int nq, int R, unsigned long long* dense, unsigned int* dense_count) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < (int64_t)nq * RP) dense[i] = ((unsigned long long)(i / RP) << 32) | (unsigned)(i % RP);
-    if (i == 0) *dense_count = (unsigned)((int64_t)nq * RP);
+    if (i < (int64_t)nq * R) dense[i] = ((unsigned long long)(i / R) << 32) | (unsigned)(i % R);
+    if (i == 0) *dense_count = (unsigned)((int64_t)nq * R);
 }
 
 // ------------------------------------------------------------------ host side
 size_t s3_walk_lists_bytes(int nq, int LM) {
-    return sizeof(int32_t) * (size_t)nq * (1 + LM + LM + (LM + 1)) + sizeof(uint32_t) * (size_t)nq * LM + 1024;
+    return sizeof(int32_t) * (size_t)nq * (1 + 2 * (size_t)LM) + sizeof(uint16_t) * (size_t)nq * LM * 32 + 1024;
 }
 
-int s3_walk_ranges(const ragrt_index* ix) {
-    // index ranges per walk range: one by default (4,096 passages on the benchmark corpus, about
-    // 130 touched passages per range against the table's 320-passage limit)
-    if (ix->s3_range > 0) return std::max(1, ix->s3_range >> ix->w_shift);
-    return 1;
-}
+int s3_walk_ranges(const ragrt_index*) { return 1; }
 
 size_t s3_walk_dense_bytes(const ragrt_index* ix, int nq) {
-    return sizeof(unsigned long long) * (size_t)nq * ceil_div(ix->num_ranges, 1) + 256;
+    return sizeof(unsigned long long) * (size_t)nq * ix->num_ranges + 256;
 }
 
 int s3_walk_run(ragrt_index* ix, const int32_t* topc, const float* scores, int full_scores, const int32_t* ntok,
@@ -526,8 +466,7 @@ int s3_walk_run(ragrt_index* ix, const int32_t* topc, const float* scores, int f
     int32_t* nl = (int32_t*)w;
     int32_t* lc = nl + nq;
     int32_t* lpc = lc + (size_t)nq * LM;
-    int32_t* lpo = lpc + (size_t)nq * LM;
-    uint32_t* pairs = (uint32_t*)(lpo + (size_t)nq * (LM + 1));
+    uint16_t* val = (uint16_t*)(((uintptr_t)(lpc + (size_t)nq * LM) + 15) & ~(uintptr_t)15);
 
     S3PrepParams pp;
     pp.topc = topc;
@@ -547,45 +486,38 @@ int s3_walk_run(ragrt_index* ix, const int32_t* topc, const float* scores, int f
     pp.nl = nl;
     pp.lc = lc;
     pp.lpc = lpc;
-    pp.lpo = lpo;
-    pp.pairs = pairs;
+    pp.val = val;
     pp.stats = ix->stats;
     const size_t psmem = sizeof(uint64_t) * next_pow2(LM);
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s3_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
     s3_prep<<<nq, kPrepThreads, psmem, stream>>>(pp);
     RAGRT_LAUNCH_CHECK();
 
-    const int m = s3_walk_ranges(ix);
-    const int RP = (int)ceil_div(ix->num_ranges, m);
-    int rcap_log2 = 9;
-    while (rcap_log2 > 8 && walk_smem_bytes(LM, 1 << rcap_log2) > 227 * 1024) --rcap_log2;
-    const bool fits = walk_smem_bytes(LM, 1 << rcap_log2) <= 227 * 1024;
-    if (ix->s3_mode == 1 || !fits) {     // per-token only: queue every range block for s3_accumulate
-        s3_queue_all<<<(unsigned)ceil_div((int64_t)nq * RP, 256), 256, 0, stream>>>(nq, RP, dense, dense_count);
+    const int R = ix->num_ranges;
+    const size_t smem = bucket_smem_bytes(LM);
+    const bool fits = ix->w_shift <= 12 && LM <= kBkMaxLists && smem <= 227 * 1024;
+    if (ix->s3_mode == 1 || !fits) {     // per-token only: queue every range for s3_accumulate
+        s3_queue_all<<<(unsigned)ceil_div((int64_t)nq * R, 256), 256, 0, stream>>>(nq, R, dense, dense_count);
         RAGRT_LAUNCH_CHECK();
         return RAGRT_OK;
     }
 
-    S3WalkParams p;
+    S3BucketParams p;
     p.packed = ix->d.csr_packed_24;
     p.preds = ix->d.doc_predicates;
     p.boff = ix->boff;
     p.cstart = ix->cstart;
     p.N = ix->d.num_passages;
-    p.R = ix->num_ranges;
+    p.R = R;
     p.w_shift = ix->w_shift;
-    p.m = m;
-    p.RP = RP;
     p.nl = nl;
     p.lc = lc;
     p.lpc = lpc;
-    p.lpo = lpo;
-    p.pairs = pairs;
+    p.val = val;
     p.LM = LM;
     p.masks = ix->d.doc_predicates ? masks : nullptr;
     p.q0 = q0;
     p.nq = nq;
-    p.rcap_log2 = rcap_log2;
     p.pool = pool;
     p.pool_cap = ix->d.num_passages;
     p.pool_count = pool_count;
@@ -593,18 +525,17 @@ int s3_walk_run(ragrt_index* ix, const int32_t* topc, const float* scores, int f
     p.dense = dense;
     p.dense_count = dense_count;
     p.stats = ix->stats;
-    const size_t smem = walk_smem_bytes(LM, 1 << p.rcap_log2);
-    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s3_walk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s3_bucket, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
-    RAGRT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, s3_walk, kWalkThreads, smem));
+    RAGRT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, s3_bucket, kBkThreads, smem));
     per_sm = std::max(1, per_sm);
     const int64_t ctas = (int64_t)per_sm * num_sms();
-    int rpj = 16;
-    while (rpj > 2 && (int64_t)nq * ((p.RP + rpj - 1) / rpj) < 8 * ctas) rpj >>= 1;
+    int rpj = 8;
+    while (rpj > 1 && (int64_t)nq * ((R + rpj - 1) / rpj) < 8 * ctas) rpj >>= 1;
     p.rpj = rpj;
-    const int64_t jobs = (int64_t)nq * ((p.RP + rpj - 1) / rpj);
+    const int64_t jobs = (int64_t)nq * ((R + rpj - 1) / rpj);
     const int grid = (int)std::min<int64_t>(jobs, ctas);
-    s3_walk<<<grid, kWalkThreads, smem, stream>>>(p);
+    s3_bucket<<<grid, kBkThreads, smem, stream>>>(p);
     RAGRT_LAUNCH_CHECK();
     return RAGRT_OK;
 }
