@@ -29,8 +29,9 @@
 //                   value rows of the passage's lists with 16-byte loads, then sum the 32
 //                   maxima exactly (fixed point, 2^-24 units), round once to fp32 and emit the
 //                   ranking key into the query's pool, as the per-token kernel does.
-//              A range whose entries exceed the staging area is pushed to a queue and handled
-//              by the per-token kernel (s3_accumulate in queue mode), which has no such limit.
+//              A range whose entries or touched passages exceed the staging area is pushed to a
+//              queue and handled by the per-token kernel (s3_accumulate in queue mode), which has
+//              no such limit.
 //
 // Both kernels produce bit-identical sums (the per-(passage, token) maximum is order-free and the
 // sum is exact), so the split between them never changes a result.
@@ -48,6 +49,8 @@ constexpr int kBkThreads = kBkWarps * 32;
 constexpr int kBkMaxW = 4096;             // passages per pid range (12-bit local pids)
 constexpr int kBkMaxLists = 1024;         // distinct lists per query (10-bit list ids)
 constexpr int kBkStage = 3072;            // entries per range held in shared memory
+constexpr int kBkTouched = 1024;          // touched passages per range held in shared memory
+constexpr int kBkSmemLists = 256;         // queries with at most this many lists keep their value rows in smem
 constexpr int kBatch = 2;                 // 32-entry chunks whose pid loads a warp issues together
 constexpr int kUnit = 32 * kBatch;        // entries of one list group per work unit of a warp
 constexpr uint32_t kNoEntry = 0xFFFFFFFFu;
@@ -206,11 +209,13 @@ struct S3BucketParams {
 
 __host__ __device__ inline size_t align128(size_t x) { return (x + 127) & ~(size_t)127; }
 // shared memory: counters [W/2] u32 | staging [kBkStage] u32 | filed lists [kBkStage] u16 |
-// touched passages [W] u16 | their first slot [W] u16 | per list: first posting in the range
-// [LM] i64, cstart [LM] i64, centroid [LM] i32, postings [LM] i32, entry prefix [LM + 1] i32
+// touched passages [kBkTouched] u16 | their first slot [kBkTouched] u16 | value rows
+// [kBkSmemLists][32] u16 | per list: first posting in the range [LM] i64, centroid [LM] i32,
+// postings [LM] i32, entry prefix [LM + 1] i32
 __host__ __device__ inline size_t bucket_smem_bytes(int LM) {
-    return align128(4 * (kBkMaxW / 2)) + align128(4 * kBkStage) + align128(2 * kBkStage) + 2 * align128(2 * kBkMaxW) +
-           2 * align128(8 * (size_t)LM) + 2 * align128(4 * (size_t)LM) + align128(4 * (size_t)(LM + 1));
+    return align128(4 * (kBkMaxW / 2)) + align128(4 * kBkStage) + align128(2 * kBkStage) + 2 * align128(2 * kBkTouched) +
+           align128(2 * 32 * kBkSmemLists) + align128(8 * (size_t)LM) + 2 * align128(4 * (size_t)LM) +
+           align128(4 * (size_t)(LM + 1));
 }
 
 __global__ void __launch_bounds__(kBkThreads, 3)
@@ -221,16 +226,16 @@ s3_bucket(S3BucketParams p) {
     uint32_t* cnt = reinterpret_cast<uint32_t*>(sp);    sp += align128(4 * (kBkMaxW / 2));
     uint32_t* stg = reinterpret_cast<uint32_t*>(sp);    sp += align128(4 * kBkStage);
     uint16_t* srt = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkStage);
-    uint16_t* tpp = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkMaxW);
-    uint16_t* tpo = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkMaxW);
+    uint16_t* tpp = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkTouched);
+    uint16_t* tpo = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkTouched);
+    uint4* sval = reinterpret_cast<uint4*>(sp);         sp += align128(2 * 32 * kBkSmemLists);
     int64_t* segs = reinterpret_cast<int64_t*>(sp);     sp += align128(8 * (size_t)LM);
-    int64_t* lcs = reinterpret_cast<int64_t*>(sp);      sp += align128(8 * (size_t)LM);
     int32_t* lcx = reinterpret_cast<int32_t*>(sp);      sp += align128(4 * (size_t)LM);
     int32_t* lpcx = reinterpret_cast<int32_t*>(sp);     sp += align128(4 * (size_t)LM);
     int32_t* segpre = reinterpret_cast<int32_t*>(sp);
     __shared__ int s_scan[33];
     __shared__ unsigned s_job;
-    __shared__ int s_nl, s_valid;
+    __shared__ int s_nl, s_valid, s_vsm;
     __shared__ unsigned s_touched;
     __shared__ unsigned long long s_base;
 
@@ -256,12 +261,18 @@ s3_bucket(S3BucketParams p) {
             const int32_t* lc = p.lc + (int64_t)qi * LM;
             const int32_t* lpc = p.lpc + (int64_t)qi * LM;
             for (int j = tid; j < nl; j += kBkThreads) {
-                const int c = lc[j];
-                lcx[j] = c;
+                lcx[j] = lc[j];
                 lpcx[j] = lpc[j];
-                lcs[j] = p.cstart[c];
             }
-            if (tid == 0) s_nl = nl;
+            const bool vsm = nl <= kBkSmemLists;             // value rows in shared memory
+            if (vsm) {
+                const uint4* gv = reinterpret_cast<const uint4*>(p.val + (int64_t)qi * LM * 32);
+                for (int i = tid; i < nl * 4; i += kBkThreads) sval[i] = gv[i];
+            }
+            if (tid == 0) {
+                s_nl = nl;
+                s_vsm = vsm;
+            }
             cached_q = qi;
             __syncthreads();
         }
@@ -281,7 +292,7 @@ s3_bucket(S3BucketParams p) {
                 const uint32_t* bo = p.boff + (int64_t)lcx[j] * (p.R + 1);
                 const int64_t hi = min((int64_t)bo[r + 1], (int64_t)lpcx[j]);
                 const int64_t lo = min((int64_t)bo[r], hi);
-                segs[j] = lcs[j] + lo;
+                segs[j] = p.cstart[lcx[j]] + lo;
                 segpre[j] = (int)(hi - lo);                  // length for now
                 mylen += (int)(hi - lo);
             }
@@ -359,7 +370,8 @@ s3_bucket(S3BucketParams p) {
                             unsigned tb = 0;
                             if (fm && lane == 0) tb = atomicAdd(&s_touched, (unsigned)__popc(fm));
                             tb = __shfl_sync(0xFFFFFFFFu, tb, 0);
-                            if (first) tpp[tb + __popc(fm & ((1u << lane) - 1u))] = (uint16_t)pl;
+                            const unsigned ti = tb + __popc(fm & ((1u << lane) - 1u));
+                            if (first && ti < (unsigned)kBkTouched) tpp[ti] = (uint16_t)pl;
                             if (e < e_end) stg[gb + e] = word;
                         }
                     }
@@ -367,6 +379,17 @@ s3_bucket(S3BucketParams p) {
             }
             __syncthreads();
 
+            if (s_touched > (unsigned)kBkTouched) {          // too many passages: the per-token kernel
+                for (int i = tid; i < (W >> 1); i += kBkThreads) cnt[i] = 0u;
+                if (tid == 0) {
+                    const unsigned pos = atomicAdd(p.dense_count, 1u);
+                    p.dense[pos] = ((unsigned long long)qi << 32) | (unsigned)r;
+                    if (p.stats) atomicAdd(&p.stats[7], 1ull);
+                }
+                __syncthreads();
+                if (tid == 0) s_touched = 0;
+                continue;
+            }
             // ---- C. offsets of the touched passages' entries (written over their counters)
             {
                 const int T = (int)s_touched;
@@ -411,12 +434,16 @@ s3_bucket(S3BucketParams p) {
                     if (ti < T) {
                         const int a = tpo[ti], b = ti + 1 < T ? tpo[ti + 1] : V;
                         uint4 acc = make_uint4(0u, 0u, 0u, 0u);      // fp16 bits >= 0: unsigned max
-                        for (int k = a; k < b; ++k) {
-                            const uint4 v = qval[(int)srt[k] * 4 + qd];              // 8 tokens, fp16 bits
+                        auto vmax = [&](const uint4 v) {
                             acc.x = __vmaxu2(acc.x, v.x);
                             acc.y = __vmaxu2(acc.y, v.y);
                             acc.z = __vmaxu2(acc.z, v.z);
                             acc.w = __vmaxu2(acc.w, v.w);
+                        };
+                        if (s_vsm) {                                // 8 tokens of row j at [4 j + qd]
+                            for (int k = a; k < b; ++k) vmax(sval[(int)srt[k] * 4 + qd]);
+                        } else {
+                            for (int k = a; k < b; ++k) vmax(qval[(int)srt[k] * 4 + qd]);
                         }
                         sum = h_fixed24((uint16_t)acc.x) + h_fixed24((uint16_t)(acc.x >> 16)) +
                               h_fixed24((uint16_t)acc.y) + h_fixed24((uint16_t)(acc.y >> 16)) +
