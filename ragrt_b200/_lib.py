@@ -46,6 +46,7 @@ _SIGS = {
     "ragrt_probe_depth": (I32, [P, I32, I32, P, P, I32, C.c_float, C.c_float, I32, I32, P, P, P]),
     "ragrt_tile_maxsim": (I32, [P, P, I32, I32, P, P, I32, P, P, P, P, P, P, P, I32, P]),
     "ragrt_tile_maxsim_exact": (I32, [P, P, I32, I32, P, P, I32, P, P, P]),
+    "ragrt_index_tile_maxsim": (I32, [P, P, P, I32, I32, P, I32, P]),
     "ragrt_final_topk": (I32, [P, P, I32, I32, P, I32, P, I32, P, P, P]),
     "ragrt_weft_search": (I32, [P, P, P, I32, I32, I32, P, I32, I32, I32, P, P, P]),
     "ragrt_weft_search_profiled": (I32, [P, P, P, I32, I32, I32, P, I32, I32, I32, P, P, P, P]),

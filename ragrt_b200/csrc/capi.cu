@@ -101,13 +101,31 @@ static int weft_search_impl(ragrt_index* ix, const void* d_Q, const int32_t* d_n
     S4Docs D{ix->d.doc_offsets, ix->d.doc_lens, ix->d.codes, ix->d.residuals, (const __half*)ix->d.centroids,
              (const __half*)ix->d.bucket_weights, ix->d.reversed_bit_map, ix->d.decomp_table, ix->d.num_passages,
              ix->d.num_centroids};
-    rc = rerank_mode == 1 ? s4_tc_launch((const __half*)d_Q, cand, B, K, D, fsc, stream)
+    D.dinv = ix->dinv;
+    rc = rerank_mode == 1 ? s4_gc_launch((const __half*)d_Q, cand, B, K, D, fsc, stream)
                           : s4_simt_launch((const __half*)d_Q, cand, B, K, D, fsc, stream);
     if (rc || (rc = mark(3))) return rc;
     rc = final_topk_launch(cand, fsc, B, K, ix->d.doc_predicates, ix->d.num_passages, d_masks, k_top, d_out_ids,
                            d_out_scores, stream);
     if (rc) return rc;
     return mark(4);
+}
+
+extern "C" int ragrt_index_tile_maxsim(ragrt_index* ix, const void* d_Q, const int32_t* d_pids, int32_t B, int32_t n,
+                                       float* d_out, int32_t mode, void* stream) {
+    RAGRT_REQUIRE(ix && d_Q, "null argument");
+    int rc = check_device(ix);
+    if (rc) return rc;
+    RAGRT_REQUIRE(B >= 1 && n >= 0, "B >= 1, n >= 0 required");
+    if (n == 0) return RAGRT_OK;
+    RAGRT_REQUIRE(d_pids && d_out, "null argument");
+    RAGRT_REQUIRE(((uintptr_t)d_Q & 15) == 0, "Q must be 16-byte aligned");
+    S4Docs D{ix->d.doc_offsets, ix->d.doc_lens, ix->d.codes, ix->d.residuals, (const __half*)ix->d.centroids,
+             (const __half*)ix->d.bucket_weights, ix->d.reversed_bit_map, ix->d.decomp_table, ix->d.num_passages,
+             ix->d.num_centroids};
+    D.dinv = ix->dinv;
+    if (mode == 1) return s4_gc_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
+    return s4_simt_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
 }
 
 extern "C" int ragrt_weft_search(ragrt_index* ix, const void* d_Q, const int32_t* d_ntok, int32_t B, int32_t nc,

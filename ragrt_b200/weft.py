@@ -256,8 +256,23 @@ class WeftIndex:
         return pids, sums, touched
 
     def tile_maxsim(self, Q, pids, mode=1):
-        return tile_maxsim(Q, pids, self.doc_offsets, self.doc_lens, self.codes, self.residuals, self.centroids,
-                           self.bucket_weights, self.rbm, self.decomp, mode=mode)
+        """Stage 4 on the bound index (the kernel the batched search runs): Q [B, 32, 128] (or
+        [32, 128]) fp16, pids [B, n] (or [n]) int32 -> f32 scores."""
+        _need_cuda(Q, pids)
+        squeeze = Q.dim() == 2
+        Q = _c(Q, torch.float16)
+        if squeeze:
+            Q = Q[None]
+            pids = pids.reshape(1, -1)
+        if Q.shape[1:] != (32, 128):
+            raise RuntimeError(f"fused MaxSim kernel reads Q as [32, 128]; got {tuple(Q.shape[1:])}")
+        pids = _c(pids, torch.int32)
+        B, n = pids.shape
+        out = torch.empty(B, n, dtype=torch.float32, device=Q.device)
+        if n:
+            _lib.check(_lib.lib().ragrt_index_tile_maxsim(self.handle, _ptr(Q), _ptr(pids), B, n, _ptr(out), int(mode),
+                                                          _stream()))
+        return out[0] if squeeze else out
 
     def final_topk(self, pids, scores, k, masks=None):
         return final_topk(pids, scores, k, preds=self.preds, masks=masks, num_preds=self.N)
