@@ -13,19 +13,19 @@
 // (stream q = candidates q, q+4, ...; chunks of 32 tokens, one candidate per chunk).  Tile k of
 // the CTA holds chunk k of every stream (128 tokens), stream q in rows / tensor-memory lanes
 // 32q..32q+31:
-//   * 2 gather warps (alternate tiles): the 128 tokens' centroid rows, 16-byte cp.async per
-//     piece, straight into a 128-byte-swizzled K-major shared-memory tile: the MMA's A operand.
-//     A ring of 4 such tiles.
-//   * 8 decoder warps (warp w: lane quadrant w % 4, tiles of parity (w - 2) / 4): the chunk's
-//     residual bytes loaded into registers (32 B per token, lane = token), expanded through a
-//     replicated byte LUT to the 128 bucket weights and written to tensor memory (tcgen05.st).
+//   * 8 decoder warps (warp w: lane quadrant w % 4, tiles of parity w / 4).  Two tiles ahead, a
+//     decoder copies its chunk's centroid rows (16-byte cp.async per piece, codes loaded a tile
+//     earlier) straight into its quadrant's rows of a 128-byte-swizzled K-major shared-memory
+//     tile: the MMA's A operand, in a ring of 4 tiles.  For the current tile it loads the
+//     chunk's residual bytes into registers (32 B per token, lane = token), expands them through
+//     a replicated byte LUT to the 128 bucket weights and writes them to tensor memory.
 //   * 1 MMA thread: per tile D = C.Q^T (A from shared memory) then D += W.Q^T (A from tensor
 //     memory), N = 32 query rows, into one of 4 accumulator slots.
 //   * 4 epilogue warps (quadrant w % 4): tcgen05.ld of the chunk's 32 tokens x 32 rows, scale
 //     by dinv, max over tokens per row (redux.sync.max.f32), running max per candidate, sum
 //     over rows after the candidate's last chunk.
-// mbarriers: cfull / cempty per gather stage, afull / aempty per decoder slot, dfull / dempty
-// per accumulator slot.  All waits are bounded; a timeout raises the device error flag, every
+// mbarriers: afull / aempty per decoder parity (the tile's gathered rows and its weights),
+// dfull / dempty per accumulator slot.  All waits are bounded; a timeout raises the device error flag, every
 // role leaves its loop, copies and MMAs in flight are awaited (bounded) and tensor memory is
 // freed.
 #include "common.cuh"
@@ -34,12 +34,10 @@
 
 namespace ragrt {
 
-constexpr int kGcGatherWarps = 2;
-constexpr int kGcDecWarp0 = kGcGatherWarps;                  // warps 2..9
-constexpr int kGcDecWarps = 8;
-constexpr int kGcMmaWarp = kGcDecWarp0 + kGcDecWarps;        // warp 10
-constexpr int kGcEpiWarp0 = kGcMmaWarp + 1;                  // warps 11..14
-constexpr int kGcThreads = (kGcEpiWarp0 + 4) * 32;           // 480
+constexpr int kGcDecWarps = 8;                               // warps 0..7
+constexpr int kGcMmaWarp = kGcDecWarps;                      // warp 8
+constexpr int kGcEpiWarp0 = kGcMmaWarp + 1;                  // warps 9..12
+constexpr int kGcThreads = (kGcEpiWarp0 + 4) * 32;           // 416
 constexpr int kGcCand = 256;
 constexpr int kGcStreams = 4;
 constexpr int kGcStages = 4;
@@ -60,7 +58,7 @@ constexpr int kGcSmMetaL = kGcSmMetaT + kGcCand * 8;
 constexpr int kGcSmTab = kGcSmMetaL + kGcCand * 4;           // rbm [256], decomp [1024], bw [4] fp16
 constexpr int kGcSmChunks = kGcSmTab + 256 + 1024 + 16;
 constexpr int kGcSmBar = kGcSmChunks + 16;
-constexpr int kGcNumBars = 2 * kGcStages + 2 * kGcASlots + 2 * kGcDSlots;
+constexpr int kGcNumBars = 2 * kGcASlots + 2 * kGcDSlots;
 constexpr int kGcSmTmem = kGcSmBar + 8 * kGcNumBars;
 constexpr int kGcSmAbort = kGcSmTmem + 4;
 constexpr int kGcSmBytes = kGcSmAbort + 4;
@@ -87,9 +85,7 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
     uint8_t* tab_dec = tab_rbm + 256;
     __half* tab_bw = reinterpret_cast<__half*>(tab_dec + 1024);
     int* s_chunks = reinterpret_cast<int*>(sm + kGcSmChunks);
-    uint64_t* cfull = reinterpret_cast<uint64_t*>(sm + kGcSmBar);
-    uint64_t* cempty = cfull + kGcStages;
-    uint64_t* afull = cempty + kGcStages;
+    uint64_t* afull = reinterpret_cast<uint64_t*>(sm + kGcSmBar);
     uint64_t* aempty = afull + kGcASlots;
     uint64_t* dfull = aempty + kGcASlots;
     uint64_t* dempty = dfull + kGcDSlots;
@@ -128,10 +124,6 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
         *reinterpret_cast<uint4*>(sm + kGcSmQ + tc::sw128_offset(row, c16, kRows)) = v;
     }
     if (tid == 0) {
-        for (int i = 0; i < kGcStages; ++i) {
-            tc::mbar_init(cfull + i, 1);
-            tc::mbar_init(cempty + i, 1);
-        }
         for (int i = 0; i < kGcASlots; ++i) {
             tc::mbar_init(afull + i, 4);
             tc::mbar_init(aempty + i, 1);
@@ -194,66 +186,33 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
         }
     };
 
-    if (warp < kGcGatherWarps) {
-        // ================================================================ centroid gather
-        const int g = warp;
-        GcCursor cur[kGcStreams];
-#pragma unroll
-        for (int q = 0; q < kGcStreams; ++q) {
-            cur[q] = GcCursor{-1, -32, 0, 0};
-            advance(cur[q], q);
-            if (g) advance(cur[q], q);
-        }
+    if (warp < kGcDecWarps) {
+        // ================================================================ decoders
+        const int q = warp & 3, par = warp >> 2;
+        const uint32_t tq = tbase + ((uint32_t)(32 * q) << 16) + kGcColA + (uint32_t)(par * 64);
+        const int lc = lane & (kGcLutCopies - 1);
         const int l16 = lane & 15, hh = lane >> 4;
-        int prev = -1;                                    // this warp's previous tile (its copies may be in flight)
-        for (int k = g; k < n_tiles; k += kGcGatherWarps) {
-            const int s = k % kGcStages;
-            if (k >= kGcStages &&
-                !tc::mbar_wait_or_abort(cempty + s, ((k / kGcStages) - 1) & 1, abort, kGcWaitLimit)) {
-                failed = true;
-                break;
-            }
-            uint8_t* dst = sm + kGcSmC + s * kGcCBytes;
-#pragma unroll
-            for (int q = 0; q < kGcStreams; ++q) {
-                const GcCursor& c = cur[q];
-                const bool live = c.ci < kGcCand;
-                const int ntv = live ? min(32, c.L - c.pos) : 0;
-                int code = (lane < ntv) ? D.codes[c.tstart + c.pos + lane] : 0;
+        // the load is only issued here; its value is checked where it is used
+        auto load_code = [&](const GcCursor& x) {
+            return (x.ci < kGcCand && x.pos + lane < x.L) ? D.codes[x.tstart + x.pos + lane] : 0;
+        };
+        // the chunk's centroid rows into this quadrant's rows of gather stage st (one commit group)
+        auto issue = [&](const GcCursor& x, int code, int st) {
+            if (x.ci < kGcCand) {
+                const int ntv = min(32, x.L - x.pos);
                 if ((unsigned)code >= (unsigned)D.NC) { bad_code = true; code = 0; }   // never gather outside C
+                uint8_t* dst = sm + kGcSmC + st * kGcCBytes;
 #pragma unroll 4
                 for (int i = 0; i < 16; ++i) {
                     const int t = 2 * i + hh;
                     const int ct = __shfl_sync(0xFFFFFFFFu, code, t);
                     if (t < ntv)
-                        tc::cp_async16(dst + tc::sw128_offset(32 * q + t, l16, 128), D.centroids + (int64_t)ct * kDim + l16 * 8);
+                        tc::cp_async16(dst + tc::sw128_offset(32 * q + t, l16, 128),
+                                       D.centroids + (int64_t)ct * kDim + l16 * 8);
                 }
-                advance(cur[q], q);
-                advance(cur[q], q);
             }
             tc::cp_async_commit();
-            if (prev >= 0) {                              // the previous tile's copies have landed
-                tc::cp_async_wait<1>();
-                tc::fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(cfull + prev % kGcStages);
-            }
-            prev = k;
-        }
-        tc::cp_async_wait<0>();                           // no copy may land after the CTA exits
-        if (prev >= 0 && !failed) {
-            tc::fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(cfull + prev % kGcStages);
-        }
-    } else if (warp < kGcMmaWarp) {
-        // ================================================================ residual decoders
-        const int q = warp & 3, par = (warp - kGcDecWarp0) >> 2;
-        const uint32_t tq = tbase + ((uint32_t)(32 * q) << 16) + kGcColA + (uint32_t)(par * 64);
-        const int lc = lane & (kGcLutCopies - 1);
-        GcCursor c{-1, -32, 0, 0};
-        advance(c, q);
-        if (par) advance(c, q);
+        };
         auto load_res = [&](const GcCursor& x, uint4& r0, uint4& r1) {
             if (x.ci < kGcCand && x.pos + lane < x.L) {
                 const uint4* src = reinterpret_cast<const uint4*>(D.residuals + (x.tstart + x.pos + lane) * 32);
@@ -264,19 +223,31 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
                 r1 = r0;
             }
         };
+        GcCursor c{-1, -32, 0, 0};
+        advance(c, q);
+        if (par) advance(c, q);
+        GcCursor cn = c;
+        advance(cn, q);
+        advance(cn, q);
+        issue(c, load_code(c), par);                      // tile par into stage par
+        int code_n = load_code(cn);
         uint4 r0, r1;
         load_res(c, r0, r1);
         for (int k = par; k < n_tiles; k += 2) {
-            GcCursor cn = c;
-            advance(cn, q);
-            advance(cn, q);
-            uint4 n0, n1;
-            load_res(cn, n0, n1);                         // the next tile's residuals, in flight meanwhile
+            // the MMAs of tile k - 2 are done with this parity's weight slot and with gather
+            // stage (k + 2) % 4, which the copies for tile k + 2 now fill
             if (k >= 2 && !tc::mbar_wait_or_abort(aempty + par, ((k - 2) >> 1) & 1, abort, kGcWaitLimit)) {
                 failed = true;
                 break;
             }
             tc::fence_after();
+            issue(cn, code_n, (k + 2) % kGcStages);
+            GcCursor cnn = cn;
+            advance(cnn, q);
+            advance(cnn, q);
+            const int code_nn = load_code(cnn);
+            uint4 n0, n1;
+            load_res(cn, n0, n1);                         // the next tile's residuals, in flight meanwhile
             if (c.ci < kGcCand) {
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
@@ -294,13 +265,18 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
                 }
                 tc::wait_st();
             }
+            tc::cp_async_wait<1>();                       // tile k's rows (issued an iteration ago) have landed
+            tc::fence_proxy_async();
             tc::fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(afull + par);
             c = cn;
+            cn = cnn;
+            code_n = code_nn;
             r0 = n0;
             r1 = n1;
         }
+        tc::cp_async_wait<0>();                           // no copy may land after the CTA exits
     } else if (warp == kGcMmaWarp) {
         // ================================================================ MMA issuer
         if (lane == 0) {
@@ -309,8 +285,7 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
             int issued = 0;
             for (int k = 0; k < n_tiles; ++k) {
                 const int s = k % kGcStages, a = k & 1, d = k & 3;
-                if (!tc::mbar_wait_or_abort(cfull + s, (k / kGcStages) & 1, abort, kGcWaitLimit) ||
-                    !tc::mbar_wait_or_abort(afull + a, (k >> 1) & 1, abort, kGcWaitLimit) ||
+                if (!tc::mbar_wait_or_abort(afull + a, (k >> 1) & 1, abort, kGcWaitLimit) ||
                     (k >= kGcDSlots && !tc::mbar_wait_or_abort(dempty + d, ((k >> 2) - 1) & 1, abort, kGcWaitLimit))) {
                     failed = true;
                     break;
@@ -330,7 +305,6 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
                     const uint32_t koffQ = (uint32_t)((kk >> 2) * (kRows * 128) + (kk & 3) * 32);
                     tc::mma_ts(td, ta + 8 * kk, tc::sw128_kmajor_desc(sQ + koffQ), idesc, 1);
                 }
-                tc::mma_commit(cempty + s);
                 tc::mma_commit(aempty + a);
                 tc::mma_commit(dfull + d);
                 issued = k + 1;
