@@ -19,13 +19,15 @@
 //     tile: the MMA's A operand, in a ring of 4 tiles.  For the current tile it loads the
 //     chunk's residual bytes into registers (32 B per token, lane = token), expands them through
 //     a replicated byte LUT to the 128 bucket weights and writes them to tensor memory.
-//   * 1 MMA thread: per tile D = C.Q^T (A from shared memory) then D += W.Q^T (A from tensor
-//     memory), N = 32 query rows, into one of 4 accumulator slots.
-//   * 4 epilogue warps (quadrant w % 4): tcgen05.ld of the chunk's 32 tokens x 32 rows, scale
-//     by dinv, max over tokens per row (redux.sync.max.f32), running max per candidate, sum
+//   * 2 MMA threads (one warp each, so the two issue streams run in parallel: the tensor-core
+//     instruction stream, not its arithmetic, bounds a tile of N = 32): per tile D1 = C.Q^T (A
+//     from shared memory) and D2 = W.Q^T (A from tensor memory), into one of 4 accumulator slot
+//     pairs.
+//   * 4 epilogue warps (quadrant w % 4): tcgen05.ld of the chunk's 32 tokens x 32 rows of D1
+//     and D2, their sum scaled by dinv, max over tokens per row (redux.sync.max.f32), running max per candidate, sum
 //     over rows after the candidate's last chunk.
-// mbarriers: afull / aempty per decoder parity (the tile's gathered rows and its weights),
-// dfull / dempty per accumulator slot.  All waits are bounded; a timeout raises the device error flag, every
+// mbarriers: afull / aempty per decoder parity (the tile's gathered rows and its weights; both
+// MMA threads release it), dfull / dempty per accumulator slot pair.  All waits are bounded; a timeout raises the device error flag, every
 // role leaves its loop, copies and MMAs in flight are awaited (bounded) and tensor memory is
 // freed.
 #include "common.cuh"
@@ -35,16 +37,16 @@
 namespace ragrt {
 
 constexpr int kGcDecWarps = 8;                               // warps 0..7
-constexpr int kGcMmaWarp = kGcDecWarps;                      // warp 8
-constexpr int kGcEpiWarp0 = kGcMmaWarp + 1;                  // warps 9..12
-constexpr int kGcThreads = (kGcEpiWarp0 + 4) * 32;           // 416
+constexpr int kGcMmaWarp = kGcDecWarps;                      // warps 8 (C . Q^T) and 9 (W . Q^T)
+constexpr int kGcEpiWarp0 = kGcMmaWarp + 2;                  // warps 10..13
+constexpr int kGcThreads = (kGcEpiWarp0 + 4) * 32;           // 448
 constexpr int kGcCand = 256;
 constexpr int kGcStreams = 4;
 constexpr int kGcStages = 4;
 constexpr int kGcASlots = 2, kGcDSlots = 4;
 constexpr uint32_t kGcColA = 0;                              // residual slot a: columns 64 a
-constexpr uint32_t kGcColD = 128;                            // accumulator slot d: columns 128 + 32 d
-constexpr uint32_t kGcTmemCols = 256;
+constexpr uint32_t kGcColD = 128;                            // accumulator slot d: D1 at 128 + 64 d, D2 32 further
+constexpr uint32_t kGcTmemCols = 512;
 constexpr uint32_t kGcWaitLimit = 1u << 24;                  // polls before a wait is declared failed
 constexpr int kGcLutCopies = 16;
 
@@ -126,10 +128,10 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
     if (tid == 0) {
         for (int i = 0; i < kGcASlots; ++i) {
             tc::mbar_init(afull + i, 4);
-            tc::mbar_init(aempty + i, 1);
+            tc::mbar_init(aempty + i, 2);
         }
         for (int i = 0; i < kGcDSlots; ++i) {
-            tc::mbar_init(dfull + i, 1);
+            tc::mbar_init(dfull + i, 2);
             tc::mbar_init(dempty + i, 4);
         }
         *abort = 0;
@@ -277,8 +279,11 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
             r1 = n1;
         }
         tc::cp_async_wait<0>();                           // no copy may land after the CTA exits
-    } else if (warp == kGcMmaWarp) {
-        // ================================================================ MMA issuer
+    } else if (warp < kGcEpiWarp0) {
+        // ================================================================ MMA issuers
+        // warp 8: D1 = C . Q^T (A: the gathered rows in shared memory); warp 9: D2 = W . Q^T
+        // (A: the weights in tensor memory).  Each commits to aempty and dfull (count 2 each).
+        const bool wpart = warp == kGcMmaWarp + 1;
         if (lane == 0) {
             const uint32_t sQ = tc::smem_u32(sm + kGcSmQ), sC = tc::smem_u32(sm + kGcSmC);
             constexpr uint32_t idesc = tc::idesc_f16_f32(128, 32);
@@ -291,19 +296,22 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
                     break;
                 }
                 tc::fence_after();
-                const uint32_t td = tbase + kGcColD + (uint32_t)(d * 32);
-                const uint32_t ta = tbase + kGcColA + (uint32_t)(a * 64);
+                const uint32_t td = tbase + kGcColD + (uint32_t)(d * 64) + (wpart ? 32u : 0u);
+                if (!wpart) {
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {          // D = C . Q^T
-                    const uint32_t koffC = (uint32_t)((kk >> 2) * (128 * 128) + (kk & 3) * 32);
-                    const uint32_t koffQ = (uint32_t)((kk >> 2) * (kRows * 128) + (kk & 3) * 32);
-                    tc::mma_ss(td, tc::sw128_kmajor_desc(sC + s * kGcCBytes + koffC), tc::sw128_kmajor_desc(sQ + koffQ),
-                               idesc, kk > 0);
-                }
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t koffC = (uint32_t)((kk >> 2) * (128 * 128) + (kk & 3) * 32);
+                        const uint32_t koffQ = (uint32_t)((kk >> 2) * (kRows * 128) + (kk & 3) * 32);
+                        tc::mma_ss(td, tc::sw128_kmajor_desc(sC + s * kGcCBytes + koffC),
+                                   tc::sw128_kmajor_desc(sQ + koffQ), idesc, kk > 0);
+                    }
+                } else {
+                    const uint32_t ta = tbase + kGcColA + (uint32_t)(a * 64);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {          // D += W . Q^T
-                    const uint32_t koffQ = (uint32_t)((kk >> 2) * (kRows * 128) + (kk & 3) * 32);
-                    tc::mma_ts(td, ta + 8 * kk, tc::sw128_kmajor_desc(sQ + koffQ), idesc, 1);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t koffQ = (uint32_t)((kk >> 2) * (kRows * 128) + (kk & 3) * 32);
+                        tc::mma_ts(td, ta + 8 * kk, tc::sw128_kmajor_desc(sQ + koffQ), idesc, kk > 0);
+                    }
                 }
                 tc::mma_commit(aempty + a);
                 tc::mma_commit(dfull + d);
@@ -330,9 +338,13 @@ s4_gc(const __half* __restrict__ Q, const int32_t* __restrict__ pids, int n, int
             const float inv_n = load_inv(en);
             if (!tc::mbar_wait_or_abort(dfull + d, (k >> 2) & 1, abort, kGcWaitLimit)) { failed = true; break; }
             tc::fence_after();
-            uint32_t acc[32];
-            tc::ld32x32(tbase + kGcColD + (uint32_t)(d * 32) + ((uint32_t)(32 * q) << 16), acc);
+            uint32_t acc[32], acc2[32];
+            const uint32_t tdq = tbase + kGcColD + (uint32_t)(d * 64) + ((uint32_t)(32 * q) << 16);
+            tc::ld32x32(tdq, acc);
+            tc::ld32x32(tdq + 32, acc2);
             tc::wait_ld();
+#pragma unroll
+            for (int r = 0; r < 32; ++r) acc[r] = __float_as_uint(__uint_as_float(acc[r]) + __uint_as_float(acc2[r]));
             tc::fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(dempty + d);
