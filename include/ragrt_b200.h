@@ -205,9 +205,8 @@ int ragrt_tile_maxsim_exact(const void* d_Q, const int32_t* d_pids, int32_t B, i
 /*
  * Stage 4 over a bound index: the fused decompress + TileMaxSim of ragrt_tile_maxsim for
  * d_pids [B, n] into d_out [B, n] f32, with the index's arrays (tile_maxsim_fused_decomp.cu:
- * 125-229).  mode 1 (tensor cores) takes the centroid and the residual parts of each doc
- * token in two MMAs (score within 1e-4 relative of the fp16 decode) with the per-token norms
- * computed at bind; mode 0 is the CUDA-core kernel.
+ * 125-229).  mode 1: the tensor-core kernel the batched search runs; mode 0: the CUDA-core
+ * kernel.
  */
 int ragrt_index_tile_maxsim(ragrt_index* index, const void* d_Q, const int32_t* d_pids, int32_t B, int32_t n,
                             float* d_out, int32_t mode, void* stream);

@@ -101,8 +101,7 @@ static int weft_search_impl(ragrt_index* ix, const void* d_Q, const int32_t* d_n
     S4Docs D{ix->d.doc_offsets, ix->d.doc_lens, ix->d.codes, ix->d.residuals, (const __half*)ix->d.centroids,
              (const __half*)ix->d.bucket_weights, ix->d.reversed_bit_map, ix->d.decomp_table, ix->d.num_passages,
              ix->d.num_centroids};
-    D.dinv = ix->dinv;
-    rc = rerank_mode == 1 ? s4_gc_launch((const __half*)d_Q, cand, B, K, D, fsc, stream)
+    rc = rerank_mode == 1 ? s4_tc_launch((const __half*)d_Q, cand, B, K, D, fsc, stream)
                           : s4_simt_launch((const __half*)d_Q, cand, B, K, D, fsc, stream);
     if (rc || (rc = mark(3))) return rc;
     rc = final_topk_launch(cand, fsc, B, K, ix->d.doc_predicates, ix->d.num_passages, d_masks, k_top, d_out_ids,
@@ -123,8 +122,7 @@ extern "C" int ragrt_index_tile_maxsim(ragrt_index* ix, const void* d_Q, const i
     S4Docs D{ix->d.doc_offsets, ix->d.doc_lens, ix->d.codes, ix->d.residuals, (const __half*)ix->d.centroids,
              (const __half*)ix->d.bucket_weights, ix->d.reversed_bit_map, ix->d.decomp_table, ix->d.num_passages,
              ix->d.num_centroids};
-    D.dinv = ix->dinv;
-    if (mode == 1) return s4_gc_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
+    if (mode == 1) return s4_tc_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
     return s4_simt_launch((const __half*)d_Q, d_pids, B, n, D, d_out, (cudaStream_t)stream);
 }
 

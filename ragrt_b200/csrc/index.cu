@@ -117,38 +117,6 @@ __global__ void k_check_codes(const int32_t* __restrict__ codes, int64_t num_tok
     if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(flags, kBadCodes);
 }
 
-// 16 threads per doc token, 8 dims each: the decoded token d = fp16(centroid[code] + bucket
-// weight) per dim (tile_maxsim_fused_decomp.cu:168-201), |d|^2 in fp32 and the Stage-4 scale
-// rsqrt(|d|^2 + 1e-12), once at bind instead of once per candidate in every search.  Codes were
-// validated before this runs.
-__global__ void k_token_norms(const int32_t* __restrict__ codes, const uint8_t* __restrict__ residuals,
-                              const __half* __restrict__ C, const __half* __restrict__ bw,
-                              const uint8_t* __restrict__ rbm, const uint8_t* __restrict__ decomp, int64_t T,
-                              float* __restrict__ dinv) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t t = i >> 4;
-    const int part = (int)(i & 15);
-    float ss = 0.f;
-    if (t < T) {
-        const int code = codes[t];
-        const uint4 cv = *reinterpret_cast<const uint4*>(C + (int64_t)code * 128 + part * 8);
-        const __half* ch = reinterpret_cast<const __half*>(&cv);
-        const uint8_t* rs = residuals + t * 32 + part * 2;
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-            const int rev = rbm[rs[b]];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float x = __half2float(__hadd(ch[4 * b + u], bw[decomp[rev * 4 + u] & 3]));
-                ss = fmaf(x, x, ss);
-            }
-        }
-    }
-#pragma unroll
-    for (int o = 8; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-    if (t < T && part == 0) dinv[t] = rsqrtf(ss + 1e-12f);
-}
-
 __global__ void k_list_offsets(const int64_t* __restrict__ bsums, const uint16_t* __restrict__ lengths,
                                int64_t num_lists, int64_t* __restrict__ off) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -292,7 +260,6 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
     TRY_ALLOC(ix->boff, sizeof(uint32_t) * (size_t)NC * (R + 1));
     TRY_ALLOC(ix->cnorm, sizeof(float) * NC);
     TRY_ALLOC(ix->cnmax, sizeof(float));
-    TRY_ALLOC(ix->dinv, sizeof(float) * (size_t)std::max<int64_t>(1, d.num_tokens));
     TRY_ALLOC(ix->stats, sizeof(unsigned long long) * RAGRT_NUM_STATS);
 #undef TRY_ALLOC
     cudaMemsetAsync(flags, 0, sizeof(int), stream);
@@ -336,12 +303,6 @@ extern "C" int ragrt_index_create(const ragrt_index_desc* desc, ragrt_index** ou
                                                                           d.num_passages, flags);
     k_range_offsets<<<(unsigned)ceil_div((int64_t)NC * (R + 1), T), T, 0, stream>>>(
         d.csr_packed_24, ix->cstart, ix->clists, d.csr_row_ptrs, ix->list_off, NC, R, ws, ix->boff);
-    if (d.num_tokens > 0) {
-        const int64_t thr = d.num_tokens * 16;
-        k_token_norms<<<(unsigned)ceil_div(thr, 256), 256, 0, stream>>>(
-            d.codes, d.residuals, (const __half*)d.centroids, (const __half*)d.bucket_weights, d.reversed_bit_map,
-            d.decomp_table, d.num_tokens, ix->dinv);
-    }
     if (s2_norms_launch((const __half*)d.centroids, NC, ix->cnorm, ix->cnmax, stream) != RAGRT_OK) {
         cudaFree(flags);
         return cleanup(RAGRT_ERR_CUDA);
@@ -365,7 +326,6 @@ extern "C" int ragrt_index_destroy(ragrt_index* ix) {
     cudaFree(ix->boff);
     cudaFree(ix->cnorm);
     cudaFree(ix->cnmax);
-    cudaFree(ix->dinv);
     cudaFree(ix->stats);
     cudaFree(ix->ws.base);
     delete ix;

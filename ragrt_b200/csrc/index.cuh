@@ -22,7 +22,6 @@ struct ragrt_index {
     uint32_t* boff = nullptr;      // [NC, R + 1] first posting (relative to cstart) with pid >= r*W
     float* cnorm = nullptr;        // [NC] |c|_2 of each centroid, rounded up
     float* cnmax = nullptr;        // [1] max over cnorm
-    float* dinv = nullptr;         // [num_tokens] 1 / sqrt(|d_t|^2 + 1e-12) of every decoded doc token
 
     ragrt_workspace ws;
     unsigned long long* stats = nullptr;   // [RAGRT_NUM_STATS]

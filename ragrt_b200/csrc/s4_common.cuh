@@ -16,7 +16,6 @@ struct S4Docs {
     int N;
     int NC;           // centroid rows (codes outside [0, NC) are rejected in-kernel); INT32_MAX = unchecked
     const __half* emb = nullptr;   // raw fp16 doc-token embeddings [T, 128]: exact MaxSim, no decode
-    const float* dinv = nullptr;   // [T] per-token 1 / |d| computed at index bind (s4_gc)
 };
 
 int s4_simt_launch(const __half* Q, const int32_t* pids, int B, int n, const S4Docs& D, float* out,
@@ -24,10 +23,6 @@ int s4_simt_launch(const __half* Q, const int32_t* pids, int B, int n, const S4D
 // D.emb != nullptr: exact MaxSim over raw fp16 doc-token embeddings (sum_r max_t q_r . d_t,
 // no decompression, no normalisation)
 int s4_tc_launch(const __half* Q, const int32_t* pids, int B, int n, const S4Docs& D, float* out,
-                 cudaStream_t stream);
-// Stage 4 of a bound index: centroid rows gathered into shared memory as the MMA's A operand,
-// residual weights decoded into tensor memory, per-token norms from D.dinv (s4_gc.cu)
-int s4_gc_launch(const __half* Q, const int32_t* pids, int B, int n, const S4Docs& D, float* out,
                  cudaStream_t stream);
 int final_topk_launch(const int32_t* pids, const float* scores, int B, int n, const uint32_t* preds, int num_preds,
                       const uint32_t* masks, int k, int32_t* out_ids, float* out_scores, cudaStream_t stream);
