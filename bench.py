@@ -35,6 +35,7 @@ import subprocess
 import sys
 import threading
 import time
+import warnings
 
 import numpy as np
 import torch
@@ -220,10 +221,9 @@ def make_index(cents, corp, shard, ix):
 
 
 # ----------------------------------------------------------------------------- reference arm (CPU)
-def host_oracle_index(cents, corp, shard, ix):
-    """Host copy of the bound index for the CPU restatement (oracle/)."""
-    from oracle import oracle as O
-    host = {
+def host_arrays(cents, corp, shard, ix):
+    """Host (numpy) copies of the bound index arrays, with the bind_index names."""
+    return {
         "csr_row_ptrs": ix["csr_row_ptrs"].cpu().numpy(), "csr_col_eids": ix["csr_col_eids"].cpu().numpy(),
         "csr_block_sums": ix["csr_block_sums"].cpu().numpy(),
         "csr_lengths": ix["csr_lengths"].cpu().view(torch.int16).numpy().view(np.uint16),
@@ -234,7 +234,87 @@ def host_oracle_index(cents, corp, shard, ix):
         "reversed_bit_map": corp["reversed_bit_map"].cpu().numpy(), "decomp_table": corp["decomp_table"].cpu().numpy(),
         "doc_predicates": shard["preds"].cpu().to(torch.int64).numpy().astype(np.uint32),
     }
-    return O.Index(host)
+
+
+def torch_reference_step(host, cfg, Q, masks, sample, K, nthreads):
+    """The reference's torch path for `sample` queries of a batch on the host cores; returns
+    seconds.  Stage 2 is the reference's weft_prep.native_prep computation itself (fp16 Q @ C^T,
+    topk(nc + 1), the (nc+1)-th score subtracted: src/weft_prep.py:32-47).  Stages 1-3 follow
+    the reference test's centroid-interaction rule (tests/test_gpu_kernels.py:259-263: per token
+    the max over its probed lists holding the passage, summed over tokens) with the kernels'
+    fp16 base scores and base > 0 rule, scattered per token over the posting lists instead of a
+    dense passage x centroid matrix, which a corpus of this size does not allow; top-K by a stable
+    sort.  Stage 4 is the test's fp32 rerank (tests/test_gpu_kernels.py:294-305: fp16 decode,
+    fp32 normalise, Q @ D^T, max over tokens, sum), over a query's candidates at once."""
+    torch.set_num_threads(nthreads)
+    nc, k_top = cfg["nc"], cfg["k_top"]
+    C = torch.from_numpy(host["centroids"])
+    lens = torch.from_numpy(host["csr_lengths"].astype(np.int64))
+    list_off = torch.zeros(lens.numel() + 1, dtype=torch.int64)
+    list_off[1:] = torch.cumsum(lens, 0)
+    row0 = torch.from_numpy(host["csr_row_ptrs"][0])
+    pk = host["csr_packed_24"].reshape(-1, 3).astype(np.int64)
+    pids = torch.from_numpy(pk[:, 0] | (pk[:, 1] << 8) | (pk[:, 2] << 16))
+    offs = torch.from_numpy(host["doc_offsets"])
+    dl = torch.from_numpy(host["doc_lens"].astype(np.int64))
+    codes = torch.from_numpy(host["codes"].astype(np.int64))
+    res = torch.from_numpy(host["residuals"])
+    bw = torch.from_numpy(host["bucket_weights"])
+    buck = torch.from_numpy(host["decomp_table"].astype(np.int64))[torch.from_numpy(host["reversed_bit_map"].astype(np.int64))]
+    preds = torch.from_numpy(host["doc_predicates"].astype(np.int64))
+    N = dl.numel()
+    Qc = Q[:sample].cpu()
+    mk = masks[:sample].cpu().tolist() if masks is not None else [0] * sample
+    t0 = time.time()
+    for b in range(sample):
+        q = Qc[b]
+        s = q @ C.T                                              # native_prep, fp16
+        vals, idx = s.topk(nc + 1, dim=-1)
+        topc = idx[:, :nc]
+        scores = vals[:, :nc].float() - vals[:, nc].float()[:, None]
+        total = torch.zeros(N)
+        touched = torch.zeros(N, dtype=torch.bool)
+        for t in range(32):
+            best = torch.zeros(N)
+            for j in range(nc):
+                base = float(scores[t, j])
+                if not base > 0.0:                               # MIN_BASE_SCORE
+                    continue
+                c = int(topc[t, j])
+                p = pids[list_off[row0[c]]:list_off[row0[c + 1]]]
+                if mk[b]:
+                    p = p[(preds[p] & mk[b]) != 0]
+                v = float(torch.tensor(base).half())             # fp16 base score
+                best[p] = torch.maximum(best[p], torch.tensor(v))
+                touched[p] = True
+            total += best
+        cand = torch.nonzero(touched).flatten()
+        if cand.numel() > K:
+            order = torch.sort(-total[cand], stable=True).indices[:K]   # score desc, pid asc
+            cand = cand[order]
+        # Stage 4: fp16 decode, fp32 normalise, max over tokens, sum over rows
+        cl = dl[cand]
+        tok = torch.repeat_interleave(offs[cand], cl) + (torch.arange(int(cl.sum())) -
+                                                        torch.repeat_interleave(torch.cumsum(cl, 0) - cl, cl))
+        D = (C[codes[tok]] + bw[buck[res[tok].long()].view(-1, 128)]).float()
+        D = D / D.norm(dim=1, keepdim=True)
+        S = (q.float() @ D.T).T                                  # [tokens, 32]
+        seg = torch.repeat_interleave(torch.arange(cand.numel()), cl)
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")                      # index_reduce_ is marked beta
+            mx = torch.full((cand.numel(), 32), -float("inf")).index_reduce_(0, seg, S, "amax")
+        f = mx.sum(1)
+        if mk[b]:
+            f[(preds[cand] & mk[b]) == 0] = -float("inf")
+        order = torch.sort(-f, stable=True).indices[:k_top]
+        _ = cand[order]
+    return time.time() - t0
+
+
+def host_oracle_index(cents, corp, shard, ix):
+    """Host copy of the bound index for the CPU restatement (oracle/)."""
+    from oracle import oracle as O
+    return O.Index(host_arrays(cents, corp, shard, ix))
 
 
 def oracle_step(oix, cfg, E, Q, masks, sample, nthreads, K=None):
@@ -340,7 +420,8 @@ def run_ours(args, cfg, rank, world, local):
     stream = torch.cuda.current_stream()
 
     # events at the stage boundaries of every timed step, on the launching stream
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(nb)]
+    nev = 5 if world == 1 else 7
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(nb)]
 
     def step(i):
         if world == 1:
@@ -397,8 +478,19 @@ def run_ours(args, cfg, rank, world, local):
     e2e = B * args.steps / (ms_e2e / 1000.0)
 
     # ---- stage breakdown of the timed steps (events recorded inside the timed region)
-    stage_ms = np.array([[ev[i][s].elapsed_time(ev[i][s + 1]) for s in range(4)] for i in range(args.warmup, nb)])
-    stage_ms = stage_ms.mean(0)
+    # per rank, mean over the timed steps; then the max over ranks of every interval
+    stage_ms = np.array([[ev[i][s].elapsed_time(ev[i][s + 1]) for s in range(nev - 1)]
+                         for i in range(args.warmup, nb)]).mean(0)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor(stage_ms, dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        stage_ms = t.cpu().numpy()
+        # 0 Stage 2 (this rank's query slice), 1 probe all-gather, 2 Stages 1-3, 3 Stage 4,
+        # 4 local top-k, 5 top-k all-gather + merge
+        idx = {"s2": 0, "s3": 2, "s4": 3, "topk": 4}
+    else:
+        idx = {"s2": 0, "s3": 1, "s4": 2, "topk": 3}
     # Stage-4 algorithmic work per launch: candidates and their doc tokens, averaged over the
     # timed batches (recomputed after the timed region)
     # (the distinct-postings statistic needs an extra kernel, so it is counted here, outside the
@@ -421,19 +513,27 @@ def run_ours(args, cfg, rank, world, local):
     s3_bytes = (3.0 * st2["distinct_postings"] + 8.0 * st2["touched"]) / args.steps
     s4_bytes = 36.0 * cand_tokens + 16.0 * n_cand
     stages = {
-        "s2_centroid_topk": {"ms": stage_ms[0], "achieved": s2_flops / (stage_ms[0] / 1e3) / 1e12,
+        "s2_centroid_topk": {"ms": stage_ms[idx["s2"]], "achieved": s2_flops / (stage_ms[idx["s2"]] / 1e3) / 1e12,
                              "unit": "TFLOP/s", "peak": peaks["bf16_tflops"], "bound": "tensor",
                              "work": f"{s2_flops / 1e9:.1f} GFLOP/step"},
-        "s3_aggregate": {"ms": stage_ms[1], "achieved": s3_bytes / (stage_ms[1] / 1e3) / 1e9, "unit": "GB/s",
+        "s3_aggregate": {"ms": stage_ms[idx["s3"]], "achieved": s3_bytes / (stage_ms[idx["s3"]] / 1e3) / 1e9,
+                         "unit": "GB/s",
                          "peak": peaks["hbm_gbs"], "bound": "hbm",
                          "work": f"{s3_bytes / 1e6:.1f} MB/step (3 B x distinct postings + 8 B x touched)",
                          "algorithmic": s3_bytes / 1e9},
-        "s4_maxsim": {"ms": stage_ms[2], "achieved": s4_bytes / (stage_ms[2] / 1e3) / 1e9, "unit": "GB/s",
+        "s4_maxsim": {"ms": stage_ms[idx["s4"]], "achieved": s4_bytes / (stage_ms[idx["s4"]] / 1e3) / 1e9,
+                      "unit": "GB/s",
                       "peak": peaks["hbm_gbs"], "bound": "hbm",
                       "work": f"{s4_bytes / 1e6:.1f} MB/step (36 B x {cand_tokens:,} doc tokens + 16 B x cand)",
-                      "doc_tokens_per_s": cand_tokens / (stage_ms[2] / 1e3), "algorithmic": s4_bytes / 1e9},
-        "final_topk": {"ms": stage_ms[3]},
+                      "doc_tokens_per_s": cand_tokens / (stage_ms[idx["s4"]] / 1e3), "algorithmic": s4_bytes / 1e9},
+        "final_topk": {"ms": stage_ms[idx["topk"]]},
     }
+    if world > 1:
+        pb = 8.0 * B * 32 * nc                     # (centroid id, score) words of the whole batch
+        stages["probe_allgather"] = {"ms": stage_ms[1], "bytes_gathered": pb,
+                                     "gbs_per_rank": pb * (world - 1) / world / (stage_ms[1] / 1e3) / 1e9}
+        stages["topk_allgather_merge"] = {"ms": stage_ms[5], "bytes_gathered": 8.0 * world * B * k_top}
+    limiter = max(stages, key=lambda k: stages[k]["ms"])
     for s in stages.values():
         if "achieved" in s:
             s["frac"] = s["achieved"] / s["peak"]
@@ -450,7 +550,7 @@ def run_ours(args, cfg, rank, world, local):
                 "algorithmic": d.get("algorithmic"), "kernel": dom, "peak_source": peak_kind,
                 "timing": "CUDA events at stage boundaries inside the timed region, mean over steps"}
 
-    cpu = parity = None
+    cpu = parity = cpu_torch = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         nthreads = os.cpu_count() or 1
         sample = max(1, min(B, args.cpu_sample or nthreads))
@@ -461,6 +561,11 @@ def run_ours(args, cfg, rank, world, local):
                          f"OpenMP over queries)"}
         # parity of the benchmarked configuration: the same queries through our path
         parity = parity_check(wix, oix, cfg, ix["E"], Q[args.warmup], masks, K, sample, oids, osc, nthreads)
+        ts = max(1, args.torch_sample)
+        dtt = torch_reference_step(host_arrays(cents, corp, shard, ix), cfg, Q[args.warmup], masks, ts, K, nthreads)
+        cpu_torch = {"value": ts / dtt, "unit": "queries/s", "cores": nthreads, "kind": "reference-torch",
+                     "sample": f"{ts} queries of one batch ({dtt:.1f} s): the reference's native_prep (fp16 "
+                               f"matmul + topk) and its tests' Stage-3 / Stage-4 formulas in torch on the host"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
@@ -476,7 +581,10 @@ def run_ours(args, cfg, rank, world, local):
             "stages": {k: {kk: (round(vv, 4) if isinstance(vv, float) else vv) for kk, vv in v.items()}
                        for k, v in stages.items()},
             "stage4_doc_tokens_per_s": stages["s4_maxsim"]["doc_tokens_per_s"],
+            "limiter": {"stage": limiter, "ms": stages[limiter]["ms"],
+                        "note": "per-rank stage times, mean over the timed steps, max over ranks"},
             "cpu_baseline": cpu,
+            "cpu_baseline_torch": cpu_torch,
             "parity": parity,
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
@@ -498,6 +606,7 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg3")
     ap.add_argument("--cpu-sample", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--torch-sample", type=int, default=4, help="queries of the torch CPU reference leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     cfg = CONFIGS[args.config]

@@ -94,9 +94,9 @@ def sharded_search(wix, Q, world, rank, pid_base, nc=32, K=4096, k_top=10, ntok=
     this rank's shard `wix` (local pids + pid_base), then the merge over ranks.  `ntok` (int32
     [B], optional) limits the query tokens of Stages 2-3 as in WeftIndex.search; Stage 4 scores
     all 32 rows of Q, as the single-GPU search does.  Returns (global pids int64 [B, k_top],
-    scores f32 [B, k_top]), the same on every rank.  `events`: optional 5 torch.cuda.Event
-    recorded before Stage 2, after the probe exchange, after Stages 1-3, after Stage 4 and
-    after the local top-k."""
+    scores f32 [B, k_top]), the same on every rank.  `events`: optional 7 torch.cuda.Event
+    recorded before Stage 2, after Stage 2, after the probe all-gather, after Stages 1-3, after
+    Stage 4, after the local top-k and after the top-k all-gather and merge."""
     def mark(i):
         if events is not None:
             events[i].record()
@@ -115,12 +115,15 @@ def sharded_search(wix, Q, world, rank, pid_base, nc=32, K=4096, k_top=10, ntok=
             nts[:hi - lo] = ntok[lo:hi]
     mark(0)
     topc, sc, _, _ = wix.centroid_topk(Qs, nc, ntok=nts)
-    topc, sc = gather_probes(topc, sc, world, B, group=group)
     mark(1)
-    pids, _, _ = wix.candidates(topc, sc, K, ntok=ntok, masks=masks)
+    topc, sc = gather_probes(topc, sc, world, B, group=group)
     mark(2)
-    f = wix.tile_maxsim(Q, pids)
+    pids, _, _ = wix.candidates(topc, sc, K, ntok=ntok, masks=masks)
     mark(3)
-    ids, s = wix.final_topk(pids, f, k_top, masks=masks)
+    f = wix.tile_maxsim(Q, pids)
     mark(4)
-    return merge_topk(ids, s, world, k_top, pid_base, group=group)
+    ids, s = wix.final_topk(pids, f, k_top, masks=masks)
+    mark(5)
+    out = merge_topk(ids, s, world, k_top, pid_base, group=group)
+    mark(6)
+    return out
