@@ -115,6 +115,11 @@ class ClockSampler:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes up to a second to start: wait for its first sample, so that the
+            # (sub-second) timed region is sampled
+            deadline = time.time() + 10.0
+            while not self.out and self.proc.poll() is None and time.time() < deadline:
+                time.sleep(0.01)
         except FileNotFoundError:
             self.proc = None
         return self

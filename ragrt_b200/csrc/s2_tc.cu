@@ -12,13 +12,17 @@
 //            tcgen05.ld and release it.  Each fp32 accumulation brackets the exact fp16 score:
 //            lo = RN16(acc - eps) <= RN16(exact) <= hi = RN16(acc + eps) (s2_common.cuh).
 //            Lane l filters its row's 128 scores against the row's admission key Te (a
-//            lower bound on the row's final kk-th key); rows with survivors are then taken
-//            one at a time by the whole warp, lane = centroid, which appends superset keys
-//            (lo, centroid asc, bit 0 = "lo != hi") to the row's 64-slot list.  A full list
-//            is compacted warp-wide: bitonic sort, T = kk-th lower-bound key, keep the first
-//            kk and the entries whose upper bound still beats T (if none can be dropped,
-//            the ambiguous ones are resolved with an exact fp64 dot product first).  T is
-//            published per row with atomicMax, so the slices of a row share one admission key.
+//            lower bound on the row's final kk-th key); rows with survivors in a 32-column
+//            chunk are then taken one at a time by the whole warp, lane = centroid, which
+//            appends raw entries (fp32 accumulation, centroid) to the row's 64-slot list.  A
+//            full list is settled -- raw entries become superset keys (lo, centroid asc, bit 0 =
+//            "lo != hi"), those whose upper bound cannot beat Te are dropped -- and compacted
+//            warp-wide: bitonic sort, T = kk-th lower-bound key, keep the first kk and the
+//            entries whose upper bound still beats T (if none can be dropped, the ambiguous ones
+//            are resolved with an exact fp64 dot product first).  T is published per row with
+//            atomicMax, so the slices of a row share one admission key.  The path taken on
+//            tiles with survivors is kept small (rolled loops) so that it stays in the
+//            instruction cache.
 // Each CTA writes its rows' sorted supersets to partial[query][slice][token][64];
 // s2_merge_tc takes the global superset across slices, resolves only its ambiguous
 // members with an exact fp64 dot product and selects the exact top-kk.  All waits are
@@ -36,7 +40,8 @@ namespace ragrt {
 constexpr int kQM = 128;                       // query rows per CTA
 constexpr int kCN = 128;                       // centroids per tile
 constexpr int kAccBufs = 4;                    // tensor-memory accumulators (128 columns each)
-constexpr int kS2TcThreads = 192;
+constexpr int kS2TcThreads = 192;             // selecting pass: producer, MMA, 4 epilogue warps
+constexpr int kS2PreThreads = 320;             // pre-pass: producer, MMA, 2 x 4 epilogue warps
 constexpr uint32_t kTileBytes = kCN * 256;     // 32 KB: two 16 KB K-atoms
 constexpr uint32_t kQTileBytes = kQM * 256;    // 32 KB
 constexpr uint32_t kS2WaitLimit = 1u << 24;
@@ -129,6 +134,53 @@ __device__ __forceinline__ void s2_sort64_desc(uint64_t& a0, uint64_t& a1, int l
     }
 }
 
+// Raw list entry, appended by the row's lane without any per-entry work: bit 63 set, the fp32
+// accumulation in bits 31..62, the centroid id in bits 0..30.  Keys (sk_make) have bits 48..63
+// clear, so the two kinds share a list.
+__device__ __forceinline__ uint64_t raw_make(float acc, int c) {
+    return (1ull << 63) | ((uint64_t)__float_as_uint(acc) << 31) | (uint64_t)(uint32_t)c;
+}
+
+// Settle one row's list (warp-wide): turn every raw entry into its superset key -- the fp16
+// bracket lo <= RN16(exact) <= hi of its accumulation, bit 0 = "lo != hi", resolved exactly where
+// the bracket spans more than one fp16 step -- and drop the entries whose upper bound does not
+// beat the row's admission key te.
+__device__ __noinline__ void s2_settle(uint64_t* lst, int n, uint64_t te, float qn, const float* __restrict__ cnorm,
+                                       const __half* qrow, const __half* C, int lane) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int e = lane + 32 * h;
+        uint64_t a = e < n ? lst[e] : 0ull;
+        bool exact = false;
+        if (a >> 63) {
+            const float acc = __uint_as_float((uint32_t)(a >> 31));
+            const uint32_t c = (uint32_t)a & 0x7FFFFFFFu;
+            const float eps = fmaf(fabsf(acc), 1.2e-7f, qn * __ldg(cnorm + c) * kEpsTc);
+            uint16_t hi = __half_as_ushort(__float2half_rn(acc + eps));
+            if (hi == 0x8000u) hi = 0;
+            if (sk_make(hi, c, 0) <= te) {
+                a = 0ull;
+            } else {
+                uint16_t lo = __half_as_ushort(__float2half_rn(acc - eps));
+                if (lo == 0x8000u) lo = 0;
+                const uint32_t amb = lo != hi;
+                exact = amb && f16_next(lo) != hi;       // tiny scores: the bracket spans several steps
+                a = sk_make(lo, c, exact ? 0 : amb);
+            }
+        }
+        unsigned need = __ballot_sync(0xFFFFFFFFu, exact);
+        while (need) {
+            const int s = __ffs(need) - 1;
+            need &= need - 1;
+            const uint32_t id = sk_id(__shfl_sync(0xFFFFFFFFu, a, s));
+            const uint16_t hx = s2_warp_exact(qrow, C + (int64_t)id * kDim, lane);
+            if (lane == s) a = sk_make(hx, id, 0) <= te ? 0ull : sk_make(hx, id, 0);
+        }
+        if (e < n) lst[e] = a;
+    }
+    __syncwarp();
+}
+
 // Compact one row's list (warp-wide): optionally resolve every ambiguous entry exactly, sort
 // by key, take T = the kk-th lower-bound key (0 while fewer than kk entries), and keep the
 // first kk entries plus those whose upper bound beats T.  Returns T; updates n.
@@ -166,18 +218,20 @@ __device__ __noinline__ uint64_t s2_compact(uint64_t* lst, int& n, int kk, bool 
 }
 
 // kTileMax: the pre-pass.  Same GEMM; the epilogue only records, per row and 128-centroid
-// tile, RN16(max acc - eps), a lower bound of the tile's best fp16 score.
+// tile, RN16(max acc - eps), a lower bound of the tile's best fp16 score.  It keeps no lists,
+// so it runs two epilogue warp sets (4 warps each, one per lane quadrant) on alternate tiles.
 template <bool kTileMax>
-__global__ void __launch_bounds__(kS2TcThreads, 1)
+__global__ void __launch_bounds__(kTileMax ? kS2PreThreads : kS2TcThreads, 1)
 s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmC, S2TcParams p) {
+    constexpr int kSets = kTileMax ? 2 : 1;
     extern __shared__ uint8_t s2_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)s2_raw + 1023) & ~(uintptr_t)1023);
     const int S = p.stages, kk = p.kk;
     uint8_t* sA = sm;
     uint8_t* sB = sm + kQTileBytes;
     uint64_t* lists = reinterpret_cast<uint64_t*>(sB + (size_t)S * kTileBytes);    // [128 rows][kListCap]
-    float* scratch = reinterpret_cast<float*>(lists + (size_t)kListCap * kQM);     // [4 warps][32][33]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + 4 * 32 * 33);
+    float* scratch = reinterpret_cast<float*>(lists + (kTileMax ? 0 : (size_t)kListCap * kQM));  // [128][33]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + (kTileMax ? 0 : kQM * 33));   // 8-byte aligned
     uint64_t* fullA = bars;
     uint64_t* full = bars + 1;
     uint64_t* empty = full + S;
@@ -191,10 +245,12 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     const int t0 = slice * p.tiles_per_slice;
     const int ntiles = min(p.tiles_total, t0 + p.tiles_per_slice) - t0;
 
-    for (int i = threadIdx.x; i < kListCap * kQM; i += blockDim.x) lists[i] = 0ull;
+    if constexpr (!kTileMax)
+        for (int i = threadIdx.x; i < kListCap * kQM; i += blockDim.x) lists[i] = 0ull;
     if (threadIdx.x == 0) {
         tc::mbar_init(fullA, 1);
         for (int s = 0; s < S; ++s) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
+        // each tile is drained by one warp set: its 4 arrivals release the accumulator
         for (int b = 0; b < kAccBufs; ++b) { tc::mbar_init(accf + b, 1); tc::mbar_init(acce + b, 4); }
         *abort = 0;
         tc::mbar_fence_init();
@@ -250,10 +306,12 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     } else {
         // ------------------------------------------------------------ epilogue (warp-cooperative)
         // Lane l of warp (quad) owns TMEM lane 32*quad + l = one query row: it filters that
-        // row's scores with a per-row threshold.  Rows with survivors are then handled one at a
-        // time by the whole warp (lane = centroid column), appending keys to the row's list
-        // and compacting the list (bitonic sort + trim) when it is full.
+        // row's scores with a per-row threshold.  Rows with survivors in a 32-column chunk are
+        // then handled one at a time by the whole warp (lane = centroid column), which appends
+        // raw entries (accumulation, centroid) to the row's list; a full list is settled into
+        // superset keys and compacted (bitonic sort + trim) warp-wide.
         const int quad = warp & 3;
+        const int set = (warp - 2) >> 2;                // this warp set's tiles: set, set + kSets, ...
         const int r = quad * 32 + lane;
         const int grow = rb * kQM + r;
         const int qb = grow / p.rows, tok = grow % p.rows;
@@ -278,12 +336,13 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         uint64_t Te = 0;
         float thr = -INFINITY;
         unsigned long long* gT = p.gthr + (valid ? grow : 0);
-        float* sc = scratch + quad * (32 * 33);                      // [32 rows][33] of this warp
         uint64_t* wl = lists + (size_t)quad * 32 * kListCap;        // the warp's 32 row lists
-        for (int i = 0; i < ntiles; ++i) {
+        float* sc = scratch + (quad * 32 + lane) * 33;              // this lane's staged chunk scores
+        for (int i = set; i < ntiles; i += kSets) {
             const int b = i % kAccBufs;
             // other slices' progress on this row (issued before the wait to hide its latency)
-            const unsigned long long g = valid ? *reinterpret_cast<volatile unsigned long long*>(gT) : 0ull;
+            const unsigned long long g =
+                (!kTileMax && valid) ? *reinterpret_cast<volatile unsigned long long*>(gT) : 0ull;
             const bool ok = tc::mbar_wait_or_abort(accf + b, (i / kAccBufs) & 1, abort, kS2WaitLimit);
             if (!__all_sync(0xFFFFFFFFu, ok)) break;          // warp-uniform: tcgen05.ld is warp-collective
             tc::fence_after();
@@ -322,99 +381,94 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                     if (lo == 0x8000u) lo = 0;
                     p.tilemax[(int64_t)grow * p.tiles_total + t0 + i] = lo;
                 }
-                continue;
-            }
-            if (g > Te) {
-                Te = g;
-                thr = s2_filter_threshold(Te, eps_max);
-            }
+            } else {
+                if (g > Te) {
+                    Te = g;
+                    thr = s2_filter_threshold(Te, eps_max);
+                }
+                // the tile's four 32-column chunk maxima (independent trees), then one vote
+                float mx[4];
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t cand = 0;
-                if (valid) {
+                for (int ch = 0; ch < 4; ++ch) {
                     float m16[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        m16[j] = fmaxf(__uint_as_float(v[ch][j]), __uint_as_float(v[ch][j + 16]));
+                    for (int j = 0; j < 16; ++j) m16[j] = fmaxf(__uint_as_float(v[ch][j]), __uint_as_float(v[ch][j + 16]));
 #pragma unroll
                     for (int w2 = 8; w2 >= 1; w2 >>= 1)
 #pragma unroll
                         for (int j = 0; j < w2; ++j) m16[j] = fmaxf(m16[j], m16[j + w2]);
-                    if (m16[0] >= thr) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) cand |= (__uint_as_float(v[ch][j]) >= thr) ? (1u << j) : 0u;
-                    }
+                    mx[ch] = m16[0];
                 }
-                unsigned act = __ballot_sync(0xFFFFFFFFu, cand != 0);
-                if (!act) continue;
-                if (cand) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) sc[lane * 33 + j] = __uint_as_float(v[ch][j]);
-                }
-                __syncwarp();
-                while (act) {
-                    const int src = __ffs(act) - 1;
-                    act &= act - 1;
-                    // ---- row `src`, lane = centroid column c0 + 32 ch + lane
-                    const uint32_t cm = __shfl_sync(0xFFFFFFFFu, cand, src);
-                    int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
-                    uint64_t Te_s = __shfl_sync(0xFFFFFFFFu, Te, src);
-                    const float qn_s = __shfl_sync(0xFFFFFFFFu, qn, src);
-                    const __half* qrow_s = p.Q + (int64_t)(rb * kQM + quad * 32 + src) * kDim;
-                    uint64_t* lst = wl + src * kListCap;
-                    const int c = c0 + ch * 32 + lane;
-                    bool adm = ((cm >> lane) & 1u) && c < p.NC;
-                    uint64_t key = 0;
-                    if (adm) {
-                        const float acc = sc[src * 33 + lane];
-                        const float eps = fmaf(fabsf(acc), 1.2e-7f, qn_s * __ldg(p.cnorm + c) * kEpsTc);
-                        uint16_t hi = __half_as_ushort(__float2half_rn(acc + eps));
-                        if (hi == 0x8000u) hi = 0;
-                        if (sk_make(hi, (uint32_t)c, 0) <= Te_s) {
-                            adm = false;
-                        } else {
-                            uint16_t lo = __half_as_ushort(__float2half_rn(acc - eps));
-                            if (lo == 0x8000u) lo = 0;
-                            uint32_t amb = lo != hi;
-                            if (amb && f16_next(lo) != hi) {
-                                // the bracket spans more than one fp16 step (tiny scores): resolve now
-                                lo = s2_exact(qrow_s, p.C + (int64_t)c * kDim);
-                                amb = 0;
-                                if (sk_make(lo, (uint32_t)c, 0) <= Te_s) adm = false;
-                            }
-                            key = sk_make(lo, (uint32_t)c, amb);
+                const bool hit = valid && fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) >= thr;
+                if (!__any_sync(0xFFFFFFFFu, hit)) continue;
+                // The candidate path runs on a minority of tiles: it is kept small (a rolled loop over
+                // the chunks, the chunk's scores staged in this lane's scratch row) so that it stays
+                // in the instruction cache.
+#pragma unroll 1
+                for (int ch = 0; ch < 4; ++ch) {
+                    const float mxc = ch == 0 ? mx[0] : ch == 1 ? mx[1] : ch == 2 ? mx[2] : mx[3];
+                    const bool cb_hit = hit && mxc >= thr;
+                    if (!__any_sync(0xFFFFFFFFu, cb_hit)) continue;
+                    const int cb = c0 + ch * 32;
+                    // columns of this chunk that hold real centroids (the rest are zero-filled)
+                    const uint32_t colmask = cb + 32 <= p.NC ? 0xFFFFFFFFu : (cb < p.NC ? (1u << (p.NC - cb)) - 1u : 0u);
+                    if (cb_hit) {
+                        switch (ch) {
+#define RAGRT_S2_STAGE(K)                                                                  \
+    case K:                                                                                \
+        _Pragma("unroll") for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(v[K][j]);   \
+        break;
+                            RAGRT_S2_STAGE(0)
+                            RAGRT_S2_STAGE(1)
+                            RAGRT_S2_STAGE(2)
+                            RAGRT_S2_STAGE(3)
+#undef RAGRT_S2_STAGE
                         }
                     }
-                    bool raised = false;
-                    unsigned am = __ballot_sync(0xFFFFFFFFu, adm);
-                    while (am) {
-                        const int room = kListCap - n_s;
-                        if (room == 0) {
+                    uint32_t cand = 0;
+                    if (cb_hit) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) cand |= sc[j] >= thr ? (1u << j) : 0u;
+                        cand &= colmask;
+                    }
+                    __syncwarp();                                // the staged rows, visible warp-wide
+                    // ---- each row with survivors in turn, lane = column: raw entries, no per-entry work
+                    unsigned act = __ballot_sync(0xFFFFFFFFu, cand != 0);
+                    while (act) {
+                        const int src = __ffs(act) - 1;
+                        uint32_t cm = __shfl_sync(0xFFFFFFFFu, cand, src);
+                        int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
+                        uint64_t* lst = wl + src * kListCap;
+                        const int pos = n_s + __popc(cm & ((1u << lane) - 1u));
+                        const bool put = ((cm >> lane) & 1u) && pos < kListCap;
+                        if (put) lst[pos] = raw_make(scratch[(quad * 32 + src) * 33 + lane], cb + lane);
+                        const unsigned put_m = __ballot_sync(0xFFFFFFFFu, put);
+                        n_s += __popc(put_m);
+                        cm &= ~put_m;
+                        if (cm) {
+                            // the row's list is full: settle + compact it warp-wide, then place the rest
+                            __syncwarp();
+                            const uint64_t Te_s = __shfl_sync(0xFFFFFFFFu, Te, src);
+                            const float qn_s = __shfl_sync(0xFFFFFFFFu, qn, src);
+                            const __half* qrow_s = p.Q + (int64_t)(rb * kQM + quad * 32 + src) * kDim;
+                            s2_settle(lst, n_s, Te_s, qn_s, p.cnorm, qrow_s, p.C, lane);
                             uint64_t T = s2_compact(lst, n_s, kk, false, qrow_s, p.C, lane);
                             if (n_s == kListCap) T = s2_compact(lst, n_s, kk, true, qrow_s, p.C, lane);
-                            if (T > Te_s) { Te_s = T; raised = true; }
-                            if (adm && sk_hi(key) <= Te_s) adm = false;
-                            am = __ballot_sync(0xFFFFFFFFu, adm);
-                            continue;
+                            if (lane == src && T > Te) {
+                                Te = T;
+                                thr = s2_filter_threshold(Te, eps_max);
+                                atomicMax(gT, (unsigned long long)Te);
+                            }
+                        } else {
+                            act &= act - 1;
                         }
-                        const int rank = __popc(am & ((1u << lane) - 1u));
-                        const bool take = adm && rank < room;
-                        if (take) lst[n_s + rank] = key;
-                        n_s += min(__popc(am), room);
-                        adm = adm && !take;
-                        am = __ballot_sync(0xFFFFFFFFu, adm);
-                    }
-                    __syncwarp();
-                    if (raised && lane == 0) atomicMax(p.gthr + (rb * kQM + quad * 32 + src), (unsigned long long)Te_s);
-                    if (lane == src) {
-                        n = n_s;
-                        if (Te_s > Te) {
-                            Te = Te_s;
-                            thr = s2_filter_threshold(Te, eps_max);
+                        if (lane == src) {
+                            n = n_s;
+                            cand = cm;
                         }
                     }
+                    __syncwarp();                                // scratch rows are restaged by the next chunk
                 }
-                __syncwarp();
             }
         }
         // ---- every valid row: final compaction (sorted, trimmed) and write-out
@@ -423,7 +477,10 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
             const int grow_s = rb * kQM + quad * 32 + src;
             uint64_t* lst = wl + src * kListCap;
-            s2_compact(lst, n_s, kk, false, p.Q + (int64_t)grow_s * kDim, p.C, lane);
+            const __half* qrow_s = p.Q + (int64_t)grow_s * kDim;
+            s2_settle(lst, n_s, __shfl_sync(0xFFFFFFFFu, Te, src), __shfl_sync(0xFFFFFFFFu, qn, src), p.cnorm, qrow_s,
+                      p.C, lane);
+            s2_compact(lst, n_s, kk, false, qrow_s, p.C, lane);
             const int qb_s = grow_s / p.rows, tok_s = grow_s % p.rows;
             uint64_t* out = p.partial + (((int64_t)qb_s * p.nslices + slice) * p.rows + tok_s) * kListCap;
             out[lane] = lane < n_s ? lst[lane] : 0ull;
@@ -623,13 +680,13 @@ static int make_map(CUtensorMap* m, const void* base, int64_t rows) {
     return RAGRT_OK;
 }
 
-static size_t s2_tc_smem(int kk, int stages) {
-    return 1024 + kQTileBytes + (size_t)stages * kTileBytes + (size_t)kListCap * kQM * 8 + 4 * 32 * 33 * 4 +
-           8 * (1 + 2 * stages + 2 * kAccBufs) + 16;
+static size_t s2_tc_smem(bool tilemax, int stages) {
+    const size_t lists = tilemax ? 0 : (size_t)kListCap * kQM * 8 + (size_t)kQM * 33 * 4;
+    return 1024 + kQTileBytes + (size_t)stages * kTileBytes + lists + 8 * (1 + 2 * stages + 2 * kAccBufs) + 16;
 }
 
 bool s2_tc_supported(int kk, int64_t rows_total) {
-    return rows_total >= kQM && kk < kListCap && s2_tc_smem(kk, 2) <= 227 * 1024;
+    return rows_total >= kQM && kk < kListCap && s2_tc_smem(false, 2) <= 227 * 1024;
 }
 
 void s2_tc_plan(int B, int rows, int NC, int& nslices, int& tiles_per_slice) {
@@ -660,19 +717,23 @@ int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __hal
     if (rc) return rc;
     if ((rc = make_map(&tmC, C, NC))) return rc;
     int stages = 4;
-    while (stages > 2 && s2_tc_smem(kk, stages) > 227 * 1024) --stages;
-    const size_t smem = s2_tc_smem(kk, stages);
+    while (stages > 2 && s2_tc_smem(false, stages) > 227 * 1024) --stages;
+    const size_t smem = s2_tc_smem(false, stages);
+    const int pre_stages = 6;                     // the pre-pass keeps no lists: a deeper ring fits
+    const size_t pre_smem = s2_tc_smem(true, pre_stages);
     unsigned long long* gthr = reinterpret_cast<unsigned long long*>(
         partial + (size_t)B * nslices * rows * kListCap);
     const int tiles_total = (int)ceil_div(NC, kCN);
     uint16_t* tilemax = reinterpret_cast<uint16_t*>(gthr + (size_t)B * rows);
     S2TcParams p{Q, C, cnorm, cnmax, ntok, partial, gthr, tilemax, err, B * rows, rows, NC, kk, tiles_total, tps,
                  nslices, stages};
-    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    S2TcParams pp = p;
+    pp.stages = pre_stages;
+    RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pre_smem));
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(nslices, (unsigned)ceil_div((int64_t)B * rows, kQM));
     // pre-pass: per-row tile bounds -> seeded admission keys; then the selecting pass
-    s2_tc<true><<<grid, kS2TcThreads, smem, stream>>>(tmQ, tmC, p);
+    s2_tc<true><<<grid, kS2PreThreads, pre_smem, stream>>>(tmQ, tmC, pp);
     RAGRT_LAUNCH_CHECK();
     s2_seed_threshold<<<(unsigned)ceil_div((int64_t)B * rows * 32, 256), 256, 0, stream>>>(tilemax, tiles_total,
                                                                                           B * rows, kk, gthr);
