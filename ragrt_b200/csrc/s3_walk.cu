@@ -51,7 +51,7 @@ constexpr int kBkMaxLists = 1024;         // distinct lists per query (10-bit li
 constexpr int kBkStage = 3072;            // entries per range held in shared memory
 constexpr int kBkTouched = 1024;          // touched passages per range held in shared memory
 constexpr int kBkSmemLists = 256;         // queries with at most this many lists keep their value rows in smem
-constexpr int kBatch = 2;                 // 32-entry chunks whose pid loads a warp issues together
+constexpr int kBatch = 3;                 // 32-entry chunks whose pid loads a warp issues together
 constexpr int kUnit = 32 * kBatch;        // entries of one list group per work unit of a warp
 constexpr uint32_t kNoEntry = 0xFFFFFFFFu;
 
@@ -87,6 +87,34 @@ __device__ __forceinline__ int cta_excl_scan(int v, int* s, int* total) {
     *total = s[32];
     __syncthreads();
     return r;
+}
+
+// The same scan without its trailing barrier: `s` must not be written by another scan until every
+// thread has passed a later barrier (the walk alternates two scratch buffers).
+__device__ __forceinline__ int cta_excl_scan_open(int v, int* s, int* total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) s[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        int x = lane < nw ? s[lane] : 0;
+        int xi = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xFFFFFFFFu, xi, o);
+            if (lane >= o) xi += y;
+        }
+        s[lane] = xi - x;
+        if (lane == 31) s[32] = xi;
+    }
+    __syncthreads();
+    *total = s[32];
+    return s[w] + incl - v;
 }
 
 // ------------------------------------------------------------------ per-query distinct lists
@@ -233,7 +261,7 @@ s3_bucket(S3BucketParams p) {
     int32_t* lcx = reinterpret_cast<int32_t*>(sp);      sp += align128(4 * (size_t)LM);
     int32_t* lpcx = reinterpret_cast<int32_t*>(sp);     sp += align128(4 * (size_t)LM);
     int32_t* segpre = reinterpret_cast<int32_t*>(sp);
-    __shared__ int s_scan[33];
+    __shared__ int s_scan2[2][33];          // A's and C's scans alternate buffers
     __shared__ unsigned s_job;
     __shared__ int s_nl, s_valid, s_vsm;
     __shared__ unsigned s_touched;
@@ -297,7 +325,8 @@ s3_bucket(S3BucketParams p) {
                 mylen += (int)(hi - lo);
             }
             int total = 0;
-            int run = cta_excl_scan(mylen, s_scan, &total);
+            int run = cta_excl_scan_open(mylen, s_scan2[0], &total);
+            if (tid == 0) s_touched = 0;                     // every thread is past the last range's F
             for (int j = ja; j < jb; ++j) {
                 const int len = segpre[j];
                 segpre[j] = run;
@@ -398,7 +427,7 @@ s3_bucket(S3BucketParams p) {
                 int mine = 0;
                 for (int i = ta; i < tb; ++i) mine += cnt16[tpp[i]];
                 int valid = 0;
-                int run = cta_excl_scan(mine, s_scan, &valid);
+                int run = cta_excl_scan_open(mine, s_scan2[1], &valid);
                 for (int i = ta; i < tb; ++i) {
                     const int pl = tpp[i];
                     const int c = cnt16[pl];
@@ -458,10 +487,12 @@ s3_bucket(S3BucketParams p) {
                     }
                 }
             }
-            // ---- F. the touched passages' counters back to zero for the next range
-            for (int i = tid; i < (int)s_touched; i += kBkThreads) cnt16[tpp[i]] = 0;
-            __syncthreads();
-            if (tid == 0) s_touched = 0;
+            // ---- F. the touched passages' counters back to zero for the next range (ordered before
+            // its walk by the barriers of its scan)
+            {
+                const int T = (int)s_touched;
+                for (int i = tid; i < T; i += kBkThreads) cnt16[tpp[i]] = 0;
+            }
         }
     }
 }
