@@ -459,7 +459,7 @@ s3_bucket(S3BucketParams p) {
                 const int qd = lane & 3;
                 for (int t0 = w * 8; t0 < T; t0 += kBkWarps * 8) {
                     const int ti = t0 + (lane >> 2);
-                    unsigned long long sum = 0;
+                    double sum = 0.0;                               // exact: 32 fp16 values need <= 45 bits
                     if (ti < T) {
                         const int a = tpo[ti], b = ti + 1 < T ? tpo[ti + 1] : V;
                         uint4 acc = make_uint4(0u, 0u, 0u, 0u);      // fp16 bits >= 0: unsigned max
@@ -474,15 +474,20 @@ s3_bucket(S3BucketParams p) {
                         } else {
                             for (int k = a; k < b; ++k) vmax(qval[(int)srt[k] * 4 + qd]);
                         }
-                        sum = h_fixed24((uint16_t)acc.x) + h_fixed24((uint16_t)(acc.x >> 16)) +
-                              h_fixed24((uint16_t)acc.y) + h_fixed24((uint16_t)(acc.y >> 16)) +
-                              h_fixed24((uint16_t)acc.z) + h_fixed24((uint16_t)(acc.z >> 16)) +
-                              h_fixed24((uint16_t)acc.w) + h_fixed24((uint16_t)(acc.w >> 16));
+                        const uint32_t w4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+                            sum += (double)f.x;
+                            sum += (double)f.y;
+                        }
                     }
                     sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
                     sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
                     if (ti < T && qd == 0) {
-                        const float sc = __ull2float_rn(sum) * 0x1p-24f;
+                        // the exact sum rounded once: equal to the fixed-point sum (2^-24 units) of the
+                        // per-token kernel rounded to fp32
+                        const float sc = __double2float_rn(sum);
                         pool[ti] = rank_key(sc, (int32_t)(range_lo + tpp[ti]));
                     }
                 }
