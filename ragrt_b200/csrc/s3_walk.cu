@@ -50,7 +50,6 @@ constexpr int kBkMaxW = 4096;             // passages per pid range (12-bit loca
 constexpr int kBkMaxLists = 1024;         // distinct lists per query (10-bit list ids)
 constexpr int kBkStage = 3072;            // entries per range held in shared memory
 constexpr int kBkTouched = 1024;          // touched passages per range held in shared memory
-constexpr int kBkSmemLists = 256;         // queries with at most this many lists keep their value rows in smem
 constexpr int kBatch = 3;                 // 32-entry chunks whose pid loads a warp issues together
 constexpr int kUnit = 32 * kBatch;        // entries of one list group per work unit of a warp
 constexpr uint32_t kNoEntry = 0xFFFFFFFFu;
@@ -237,16 +236,18 @@ struct S3BucketParams {
 
 __host__ __device__ inline size_t align128(size_t x) { return (x + 127) & ~(size_t)127; }
 // shared memory: counters [W/2] u32 | staging [kBkStage] u32 | filed lists [kBkStage] u16 |
-// touched passages [kBkTouched] u16 | their first slot [kBkTouched] u16 | value rows
-// [kBkSmemLists][32] u16 | per list: first posting in the range [LM] i64, centroid [LM] i32,
-// postings [LM] i32, entry prefix [LM + 1] i32
+// touched passages [kBkTouched] u16 | their first slot [kBkTouched] u16 | per list: first
+// posting in the range [LM] i64, centroid [LM] i32, postings [LM] i32, entry prefix [LM + 1] i32.
+// 51.5 KB at LM = 1,024: four CTAs per SM.  (The value rows stay in global memory, read through
+// L1 / L2: holding them in shared memory costs a CTA per SM, and the walk is bound by how many
+// warps are resident, not by those reads.)
 __host__ __device__ inline size_t bucket_smem_bytes(int LM) {
     return align128(4 * (kBkMaxW / 2)) + align128(4 * kBkStage) + align128(2 * kBkStage) + 2 * align128(2 * kBkTouched) +
-           align128(2 * 32 * kBkSmemLists) + align128(8 * (size_t)LM) + 2 * align128(4 * (size_t)LM) +
-           align128(4 * (size_t)(LM + 1));
+           align128(8 * (size_t)LM) + 2 * align128(4 * (size_t)LM) + align128(4 * (size_t)(LM + 1));
 }
 
-__global__ void __launch_bounds__(kBkThreads, 3)
+constexpr int kBkCtasPerSm = 4;           // 64 registers per thread
+__global__ void __launch_bounds__(kBkThreads, kBkCtasPerSm)
 s3_bucket(S3BucketParams p) {
     extern __shared__ __align__(128) unsigned char bk_smem[];
     const int LM = p.LM;
@@ -256,14 +257,13 @@ s3_bucket(S3BucketParams p) {
     uint16_t* srt = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkStage);
     uint16_t* tpp = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkTouched);
     uint16_t* tpo = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkTouched);
-    uint4* sval = reinterpret_cast<uint4*>(sp);         sp += align128(2 * 32 * kBkSmemLists);
     int64_t* segs = reinterpret_cast<int64_t*>(sp);     sp += align128(8 * (size_t)LM);
     int32_t* lcx = reinterpret_cast<int32_t*>(sp);      sp += align128(4 * (size_t)LM);
     int32_t* lpcx = reinterpret_cast<int32_t*>(sp);     sp += align128(4 * (size_t)LM);
     int32_t* segpre = reinterpret_cast<int32_t*>(sp);
     __shared__ int s_scan2[2][33];          // A's and C's scans alternate buffers
     __shared__ unsigned s_job;
-    __shared__ int s_nl, s_valid, s_vsm;
+    __shared__ int s_nl, s_valid;
     __shared__ unsigned s_touched;
     __shared__ unsigned long long s_base;
 
@@ -292,15 +292,7 @@ s3_bucket(S3BucketParams p) {
                 lcx[j] = lc[j];
                 lpcx[j] = lpc[j];
             }
-            const bool vsm = nl <= kBkSmemLists;             // value rows in shared memory
-            if (vsm) {
-                const uint4* gv = reinterpret_cast<const uint4*>(p.val + (int64_t)qi * LM * 32);
-                for (int i = tid; i < nl * 4; i += kBkThreads) sval[i] = gv[i];
-            }
-            if (tid == 0) {
-                s_nl = nl;
-                s_vsm = vsm;
-            }
+            if (tid == 0) s_nl = nl;
             cached_q = qi;
             __syncthreads();
         }
@@ -469,11 +461,7 @@ s3_bucket(S3BucketParams p) {
                             acc.z = __vmaxu2(acc.z, v.z);
                             acc.w = __vmaxu2(acc.w, v.w);
                         };
-                        if (s_vsm) {                                // 8 tokens of row j at [4 j + qd]
-                            for (int k = a; k < b; ++k) vmax(sval[(int)srt[k] * 4 + qd]);
-                        } else {
-                            for (int k = a; k < b; ++k) vmax(qval[(int)srt[k] * 4 + qd]);
-                        }
+                        for (int k = a; k < b; ++k) vmax(qval[(int)srt[k] * 4 + qd]);   // 8 tokens of row j at [4 j + qd]
                         const uint32_t w4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
