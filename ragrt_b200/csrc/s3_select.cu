@@ -1,8 +1,10 @@
 // s3_select.cu -- exact candidate selection per query (the reference's
 // `if (L == k) copy else torch::topk(sums, k)`, optix_corr_torch_3d.cpp:578-585):
 //   U <= K : every touched passage, in ascending pid order, then (-1, -inf) padding;
-//   U  > K : the K best by (sum desc, pid asc) -- an MSB-first radix select of the K-th
-//            largest 64-bit ranking key over the pool, then a bitonic sort of the K winners.
+//   U  > K : the K best by (sum desc, pid asc) -- an MSB-first radix select over the pool's
+//            64-bit ranking keys (8-bit digits; it stops at the first digit whose boundary bucket
+//            holds exactly the keys still needed), then a
+//            bitonic sort of the K winners.
 #include "s3_common.cuh"
 
 namespace ragrt {
@@ -14,7 +16,7 @@ s3_select(const uint64_t* __restrict__ pool, int64_t cap, const unsigned long lo
     extern __shared__ uint64_t buf[];               // [next_pow2(K)]
     __shared__ unsigned hist[256];
     __shared__ uint64_t s_prefix, s_pmask;
-    __shared__ unsigned s_need, s_nsel;
+    __shared__ unsigned s_need, s_nsel, s_done;
     const int qi = blockIdx.x, q = q0 + qi;
     const int64_t U = (int64_t)counts[qi];
     const uint64_t* keys = pool + (int64_t)qi * cap;
@@ -42,9 +44,9 @@ s3_select(const uint64_t* __restrict__ pool, int64_t cap, const unsigned long lo
             }
         }
     } else {
-        if (threadIdx.x == 0) { s_prefix = 0; s_pmask = 0; s_need = (unsigned)K; s_nsel = 0; }
+        if (threadIdx.x == 0) { s_prefix = 0; s_pmask = 0; s_need = (unsigned)K; s_nsel = 0; s_done = 0; }
         __syncthreads();
-        for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int shift = 56; shift >= 0 && !s_done; shift -= 8) {
             for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
             __syncthreads();
             const uint64_t pre = s_prefix, pm = s_pmask;
@@ -63,13 +65,16 @@ s3_select(const uint64_t* __restrict__ pool, int64_t cap, const unsigned long lo
                 s_need = need - cum;
                 s_prefix = pre | ((uint64_t)d << shift);
                 s_pmask = pm | ((uint64_t)255 << shift);
+                // the boundary bucket holds exactly the keys still needed: the K winners are the keys
+                // whose masked prefix is at least the new prefix
+                if (hist[d] == need - cum) s_done = 1;
             }
             __syncthreads();
         }
-        const uint64_t kth = s_prefix;
+        const uint64_t kth = s_prefix, kmask = s_pmask;
         for (int64_t i = threadIdx.x; i < U; i += blockDim.x) {
             const uint64_t k = keys[i];
-            if (k >= kth) {
+            if ((k & kmask) >= kth) {
                 const unsigned pos = atomicAdd(&s_nsel, 1u);
                 if (pos < (unsigned)K) buf[pos] = k;
             }
