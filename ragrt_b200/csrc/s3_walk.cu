@@ -237,16 +237,16 @@ struct S3BucketParams {
 __host__ __device__ inline size_t align128(size_t x) { return (x + 127) & ~(size_t)127; }
 // shared memory: counters [W/2] u32 | staging [kBkStage] u32 | filed lists [kBkStage] u16 |
 // touched passages [kBkTouched] u16 | their first slot [kBkTouched] u16 | per list: first
-// posting in the range [LM] i64, centroid [LM] i32, postings [LM] i32, entry prefix [LM + 1] i32.
-// 51.5 KB at LM = 1,024: four CTAs per SM.  (The value rows stay in global memory, read through
+// posting in the range [LM] i64, entry prefix [LM + 1] i32.  43.5 KB at LM = 1,024: five CTAs
+// per SM.  (The value rows stay in global memory, read through
 // L1 / L2: holding them in shared memory costs a CTA per SM, and the walk is bound by how many
 // warps are resident, not by those reads.)
 __host__ __device__ inline size_t bucket_smem_bytes(int LM) {
     return align128(4 * (kBkMaxW / 2)) + align128(4 * kBkStage) + align128(2 * kBkStage) + 2 * align128(2 * kBkTouched) +
-           align128(8 * (size_t)LM) + 2 * align128(4 * (size_t)LM) + align128(4 * (size_t)(LM + 1));
+           align128(8 * (size_t)LM) + align128(4 * (size_t)(LM + 1));
 }
 
-constexpr int kBkCtasPerSm = 4;           // 64 registers per thread
+constexpr int kBkCtasPerSm = 5;           // 51 registers per thread
 __global__ void __launch_bounds__(kBkThreads, kBkCtasPerSm)
 s3_bucket(S3BucketParams p) {
     extern __shared__ __align__(128) unsigned char bk_smem[];
@@ -258,8 +258,6 @@ s3_bucket(S3BucketParams p) {
     uint16_t* tpp = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkTouched);
     uint16_t* tpo = reinterpret_cast<uint16_t*>(sp);    sp += align128(2 * kBkTouched);
     int64_t* segs = reinterpret_cast<int64_t*>(sp);     sp += align128(8 * (size_t)LM);
-    int32_t* lcx = reinterpret_cast<int32_t*>(sp);      sp += align128(4 * (size_t)LM);
-    int32_t* lpcx = reinterpret_cast<int32_t*>(sp);     sp += align128(4 * (size_t)LM);
     int32_t* segpre = reinterpret_cast<int32_t*>(sp);
     __shared__ int s_scan2[2][33];          // A's and C's scans alternate buffers
     __shared__ unsigned s_job;
@@ -285,17 +283,13 @@ s3_bucket(S3BucketParams p) {
         const int qi = (int)(job / nrb);
         const int r0 = (int)(job % nrb) * p.rpj, r1 = min(p.R, r0 + p.rpj);
         if (qi != cached_q) {
-            const int nl = p.nl[qi];
-            const int32_t* lc = p.lc + (int64_t)qi * LM;
-            const int32_t* lpc = p.lpc + (int64_t)qi * LM;
-            for (int j = tid; j < nl; j += kBkThreads) {
-                lcx[j] = lc[j];
-                lpcx[j] = lpc[j];
-            }
-            if (tid == 0) s_nl = nl;
+            if (tid == 0) s_nl = p.nl[qi];
             cached_q = qi;
             __syncthreads();
         }
+        // the query's lists: centroid and postings, read through L1 by phase A of each range
+        const int32_t* lcx = p.lc + (int64_t)qi * LM;
+        const int32_t* lpcx = p.lpc + (int64_t)qi * LM;
         const int nl = s_nl;
         const int ngroups = (nl + 31) >> 5;
         const uint32_t mask = p.masks ? p.masks[p.q0 + qi] : 0u;
