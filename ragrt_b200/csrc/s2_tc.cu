@@ -40,8 +40,7 @@ namespace ragrt {
 constexpr int kQM = 128;                       // query rows per CTA
 constexpr int kCN = 128;                       // centroids per tile
 constexpr int kAccBufs = 4;                    // tensor-memory accumulators (128 columns each)
-constexpr int kS2TcThreads = 192;             // selecting pass: producer, MMA, 4 epilogue warps
-constexpr int kS2PreThreads = 320;             // pre-pass: producer, MMA, 2 x 4 epilogue warps
+constexpr int kS2TcThreads = 320;             // producer, MMA, 2 x 4 epilogue warps (both passes)
 constexpr uint32_t kTileBytes = kCN * 256;     // 32 KB: two 16 KB K-atoms
 constexpr uint32_t kQTileBytes = kQM * 256;    // 32 KB
 constexpr uint32_t kS2WaitLimit = 1u << 24;
@@ -218,12 +217,14 @@ __device__ __noinline__ uint64_t s2_compact(uint64_t* lst, int& n, int kk, bool 
 }
 
 // kTileMax: the pre-pass.  Same GEMM; the epilogue only records, per row and 128-centroid
-// tile, RN16(max acc - eps), a lower bound of the tile's best fp16 score.  It keeps no lists,
-// so it runs two epilogue warp sets (4 warps each, one per lane quadrant) on alternate tiles.
+// tile, RN16(max acc - eps), a lower bound of the tile's best fp16 score.  Both passes run two
+// epilogue warp sets of four (one warp per lane quadrant): the pre-pass's sets take alternate
+// tiles; the selecting pass's sets take every tile and split each quadrant's 32 rows, set s
+// admitting candidates for rows 16 s .. 16 s + 15 only, so that each row list has one owner.
 template <bool kTileMax>
-__global__ void __launch_bounds__(kTileMax ? kS2PreThreads : kS2TcThreads, 1)
+__global__ void __launch_bounds__(kS2TcThreads, 1)
 s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmC, S2TcParams p) {
-    constexpr int kSets = kTileMax ? 2 : 1;
+    constexpr int kSets = kTileMax ? 2 : 1;          // tile sets
     extern __shared__ uint8_t s2_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)s2_raw + 1023) & ~(uintptr_t)1023);
     const int S = p.stages, kk = p.kk;
@@ -250,8 +251,11 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     if (threadIdx.x == 0) {
         tc::mbar_init(fullA, 1);
         for (int s = 0; s < S; ++s) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
-        // each tile is drained by one warp set: its 4 arrivals release the accumulator
-        for (int b = 0; b < kAccBufs; ++b) { tc::mbar_init(accf + b, 1); tc::mbar_init(acce + b, 4); }
+        // a tile is drained by one warp set (pre-pass) or by both (selecting pass)
+        for (int b = 0; b < kAccBufs; ++b) {
+            tc::mbar_init(accf + b, 1);
+            tc::mbar_init(acce + b, kTileMax ? 4 : 8);
+        }
         *abort = 0;
         tc::mbar_fence_init();
     }
@@ -311,7 +315,9 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         // raw entries (accumulation, centroid) to the row's list; a full list is settled into
         // superset keys and compacted (bitonic sort + trim) warp-wide.
         const int quad = warp & 3;
-        const int set = (warp - 2) >> 2;                // this warp set's tiles: set, set + kSets, ...
+        const int wset = (warp - 2) >> 2;               // warp set 0 or 1
+        const int set = kTileMax ? wset : 0;            // this warp's tiles: set, set + kSets, ...
+        const bool own = kTileMax || (lane >> 4) == wset;  // selecting pass: this lane's row is this warp's
         const int r = quad * 32 + lane;
         const int grow = rb * kQM + r;
         const int qb = grow / p.rows, tok = grow % p.rows;
@@ -346,18 +352,18 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             const bool ok = tc::mbar_wait_or_abort(accf + b, (i / kAccBufs) & 1, abort, kS2WaitLimit);
             if (!__all_sync(0xFFFFFFFFu, ok)) break;          // warp-uniform: tcgen05.ld is warp-collective
             tc::fence_after();
-            uint32_t v[4][32];
             const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kCN);
-            tc::ld32x32(taddr, v[0]);
-            tc::ld32x32(taddr + 32, v[1]);
-            tc::ld32x32(taddr + 64, v[2]);
-            tc::ld32x32(taddr + 96, v[3]);
-            tc::wait_ld();
-            tc::fence_before();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(acce + b);
             const int c0 = (t0 + i) * kCN;
             if constexpr (kTileMax) {
+                uint32_t v[4][32];
+                tc::ld32x32(taddr, v[0]);
+                tc::ld32x32(taddr + 32, v[1]);
+                tc::ld32x32(taddr + 64, v[2]);
+                tc::ld32x32(taddr + 96, v[3]);
+                tc::wait_ld();
+                tc::fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(acce + b);
                 if (valid) {
                     const int ncv = min(kCN, p.NC - c0);            // columns past NC hold zero-filled rows
                     float m4[4];
@@ -386,93 +392,104 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
                     Te = g;
                     thr = s2_filter_threshold(Te, eps_max);
                 }
-                // the tile's four 32-column chunk maxima (independent trees), then one vote
-                float mx[4];
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    float m16[16];
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t v[2][32];
+                    tc::ld32x32(taddr + 64 * h, v[0]);
+                    tc::ld32x32(taddr + 64 * h + 32, v[1]);
+                    tc::wait_ld();
+                    if (h == 1) {                               // both halves read: release the accumulator
+                        tc::fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(acce + b);
+                    }
+                    // the tile in two halves of 64 columns (32 score registers each): per half the two
+                    // 32-column chunk maxima (independent trees), then one vote
+                    float mx[2];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) m16[j] = fmaxf(__uint_as_float(v[ch][j]), __uint_as_float(v[ch][j + 16]));
+                    for (int ch = 0; ch < 2; ++ch) {
+                        float m16[16];
 #pragma unroll
-                    for (int w2 = 8; w2 >= 1; w2 >>= 1)
+                        for (int j = 0; j < 16; ++j) m16[j] = fmaxf(__uint_as_float(v[ch][j]), __uint_as_float(v[ch][j + 16]));
 #pragma unroll
-                        for (int j = 0; j < w2; ++j) m16[j] = fmaxf(m16[j], m16[j + w2]);
-                    mx[ch] = m16[0];
-                }
-                const bool hit = valid && fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) >= thr;
-                if (!__any_sync(0xFFFFFFFFu, hit)) continue;
-                // The candidate path runs on a minority of tiles: it is kept small (a rolled loop over
-                // the chunks, the chunk's scores staged in this lane's scratch row) so that it stays
-                // in the instruction cache.
+                        for (int w2 = 8; w2 >= 1; w2 >>= 1)
+#pragma unroll
+                            for (int j = 0; j < w2; ++j) m16[j] = fmaxf(m16[j], m16[j + w2]);
+                        mx[ch] = m16[0];
+                    }
+                    const bool hit = valid && own && fmaxf(mx[0], mx[1]) >= thr;
+                    if (!__any_sync(0xFFFFFFFFu, hit)) continue;
+                    // The candidate path runs on a minority of tiles: it is kept small (a rolled loop over
+                    // the chunks, the chunk's scores staged in this lane's scratch row) so that it stays
+                    // in the instruction cache.
 #pragma unroll 1
-                for (int ch = 0; ch < 4; ++ch) {
-                    const float mxc = ch == 0 ? mx[0] : ch == 1 ? mx[1] : ch == 2 ? mx[2] : mx[3];
-                    const bool cb_hit = hit && mxc >= thr;
-                    if (!__any_sync(0xFFFFFFFFu, cb_hit)) continue;
-                    const int cb = c0 + ch * 32;
-                    // columns of this chunk that hold real centroids (the rest are zero-filled)
-                    const uint32_t colmask = cb + 32 <= p.NC ? 0xFFFFFFFFu : (cb < p.NC ? (1u << (p.NC - cb)) - 1u : 0u);
-                    if (cb_hit) {
-                        switch (ch) {
+                    for (int ch = 0; ch < 2; ++ch) {
+                        const float mxc = ch == 0 ? mx[0] : mx[1];
+                        const bool cb_hit = hit && mxc >= thr;
+                        if (!__any_sync(0xFFFFFFFFu, cb_hit)) continue;
+                        const int cb = c0 + 64 * h + ch * 32;
+                        // columns of this chunk that hold real centroids (the rest are zero-filled)
+                        const uint32_t colmask = cb + 32 <= p.NC ? 0xFFFFFFFFu : (cb < p.NC ? (1u << (p.NC - cb)) - 1u : 0u);
+                        if (cb_hit) {
+                            switch (ch) {
 #define RAGRT_S2_STAGE(K)                                                                  \
-    case K:                                                                                \
-        _Pragma("unroll") for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(v[K][j]);   \
-        break;
-                            RAGRT_S2_STAGE(0)
-                            RAGRT_S2_STAGE(1)
-                            RAGRT_S2_STAGE(2)
-                            RAGRT_S2_STAGE(3)
+        case K:                                                                                \
+            _Pragma("unroll") for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(v[K][j]);   \
+            break;
+                                RAGRT_S2_STAGE(0)
+                                RAGRT_S2_STAGE(1)
 #undef RAGRT_S2_STAGE
-                        }
-                    }
-                    uint32_t cand = 0;
-                    if (cb_hit) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) cand |= sc[j] >= thr ? (1u << j) : 0u;
-                        cand &= colmask;
-                    }
-                    __syncwarp();                                // the staged rows, visible warp-wide
-                    // ---- each row with survivors in turn, lane = column: raw entries, no per-entry work
-                    unsigned act = __ballot_sync(0xFFFFFFFFu, cand != 0);
-                    while (act) {
-                        const int src = __ffs(act) - 1;
-                        uint32_t cm = __shfl_sync(0xFFFFFFFFu, cand, src);
-                        int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
-                        uint64_t* lst = wl + src * kListCap;
-                        const int pos = n_s + __popc(cm & ((1u << lane) - 1u));
-                        const bool put = ((cm >> lane) & 1u) && pos < kListCap;
-                        if (put) lst[pos] = raw_make(scratch[(quad * 32 + src) * 33 + lane], cb + lane);
-                        const unsigned put_m = __ballot_sync(0xFFFFFFFFu, put);
-                        n_s += __popc(put_m);
-                        cm &= ~put_m;
-                        if (cm) {
-                            // the row's list is full: settle + compact it warp-wide, then place the rest
-                            __syncwarp();
-                            const uint64_t Te_s = __shfl_sync(0xFFFFFFFFu, Te, src);
-                            const float qn_s = __shfl_sync(0xFFFFFFFFu, qn, src);
-                            const __half* qrow_s = p.Q + (int64_t)(rb * kQM + quad * 32 + src) * kDim;
-                            s2_settle(lst, n_s, Te_s, qn_s, p.cnorm, qrow_s, p.C, lane);
-                            uint64_t T = s2_compact(lst, n_s, kk, false, qrow_s, p.C, lane);
-                            if (n_s == kListCap) T = s2_compact(lst, n_s, kk, true, qrow_s, p.C, lane);
-                            if (lane == src && T > Te) {
-                                Te = T;
-                                thr = s2_filter_threshold(Te, eps_max);
-                                atomicMax(gT, (unsigned long long)Te);
                             }
-                        } else {
-                            act &= act - 1;
                         }
-                        if (lane == src) {
-                            n = n_s;
-                            cand = cm;
+                        uint32_t cand = 0;
+                        if (cb_hit) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) cand |= sc[j] >= thr ? (1u << j) : 0u;
+                            cand &= colmask;
                         }
+                        __syncwarp();                                // the staged rows, visible warp-wide
+                        // ---- each row with survivors in turn, lane = column: raw entries, no per-entry work
+                        unsigned act = __ballot_sync(0xFFFFFFFFu, cand != 0);
+                        while (act) {
+                            const int src = __ffs(act) - 1;
+                            uint32_t cm = __shfl_sync(0xFFFFFFFFu, cand, src);
+                            int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
+                            uint64_t* lst = wl + src * kListCap;
+                            const int pos = n_s + __popc(cm & ((1u << lane) - 1u));
+                            const bool put = ((cm >> lane) & 1u) && pos < kListCap;
+                            if (put) lst[pos] = raw_make(scratch[(quad * 32 + src) * 33 + lane], cb + lane);
+                            const unsigned put_m = __ballot_sync(0xFFFFFFFFu, put);
+                            n_s += __popc(put_m);
+                            cm &= ~put_m;
+                            if (cm) {
+                                // the row's list is full: settle + compact it warp-wide, then place the rest
+                                __syncwarp();
+                                const uint64_t Te_s = __shfl_sync(0xFFFFFFFFu, Te, src);
+                                const float qn_s = __shfl_sync(0xFFFFFFFFu, qn, src);
+                                const __half* qrow_s = p.Q + (int64_t)(rb * kQM + quad * 32 + src) * kDim;
+                                s2_settle(lst, n_s, Te_s, qn_s, p.cnorm, qrow_s, p.C, lane);
+                                uint64_t T = s2_compact(lst, n_s, kk, false, qrow_s, p.C, lane);
+                                if (n_s == kListCap) T = s2_compact(lst, n_s, kk, true, qrow_s, p.C, lane);
+                                if (lane == src && T > Te) {
+                                    Te = T;
+                                    thr = s2_filter_threshold(Te, eps_max);
+                                    atomicMax(gT, (unsigned long long)Te);
+                                }
+                            } else {
+                                act &= act - 1;
+                            }
+                            if (lane == src) {
+                                n = n_s;
+                                cand = cm;
+                            }
+                        }
+                        __syncwarp();                                // scratch rows are restaged by the next chunk
                     }
-                    __syncwarp();                                // scratch rows are restaged by the next chunk
                 }
             }
         }
         // ---- every valid row: final compaction (sorted, trimmed) and write-out
-        for (int src = 0; src < 32 && !kTileMax; ++src) {
+        for (int src = 16 * wset; src < 16 * wset + 16 && !kTileMax; ++src) {
             if (!__shfl_sync(0xFFFFFFFFu, valid, src)) continue;
             int n_s = __shfl_sync(0xFFFFFFFFu, n, src);
             const int grow_s = rb * kQM + quad * 32 + src;
@@ -733,7 +750,7 @@ int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __hal
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(nslices, (unsigned)ceil_div((int64_t)B * rows, kQM));
     // pre-pass: per-row tile bounds -> seeded admission keys; then the selecting pass
-    s2_tc<true><<<grid, kS2PreThreads, pre_smem, stream>>>(tmQ, tmC, pp);
+    s2_tc<true><<<grid, kS2TcThreads, pre_smem, stream>>>(tmQ, tmC, pp);
     RAGRT_LAUNCH_CHECK();
     s2_seed_threshold<<<(unsigned)ceil_div((int64_t)B * rows * 32, 256), 256, 0, stream>>>(tilemax, tiles_total,
                                                                                           B * rows, kk, gthr);
