@@ -16,19 +16,22 @@
 //              (fp16 bits, 0 for a token that did not probe the list); it also counts the
 //              diagnostic statistics (postings of every kept probe, distinct postings, kept
 //              probes, tasks).
-//   s3_bucket  (persistent CTAs; a work item is one query and a block of pid ranges) takes one
-//              pid range at a time and
+//   s3_bucket  (persistent CTAs, five per SM; a work item is one query and a block of pid
+//              ranges) takes one pid range at a time and
 //                A. finds each distinct list's sub-list inside the range (the index's
 //                   range-offset table) and their prefix: the range's entries;
-//                B. walks the entries once, coalesced; an entry (passage, list) takes the next
+//                B. walks the entries once, coalesced (units of three 32-entry chunks per
+//                   warp); an entry (passage, list) takes the next
 //                   slot of its passage (a 16-bit counter per passage, two per shared word), and
 //                   the entry that takes slot 0 records the passage as touched;
 //                C. scans the touched passages' counts into their offsets;
 //                D. files every entry's list under its passage (a counting sort);
 //                E. gives each touched passage four lanes, 8 tokens each, which max-reduce the
-//                   value rows of the passage's lists with 16-byte loads, then sum the 32
-//                   maxima exactly (fixed point, 2^-24 units), round once to fp32 and emit the
-//                   ranking key into the query's pool, as the per-token kernel does.
+//                   value rows of the passage's lists with 16-byte loads (from global memory,
+//                   through L1 / L2), then sum the 32 maxima exactly (fp64), round once to fp32
+//                   and emit the ranking key into the query's pool, as the per-token kernel does.
+//              The two CTA scans of a range alternate scratch buffers, and the counter reset
+//              needs no barrier of its own: eight barriers per range.
 //              A range whose entries or touched passages exceed the staging area is pushed to a
 //              queue and handled by the per-token kernel (s3_accumulate in queue mode), which has
 //              no such limit.
@@ -237,16 +240,16 @@ struct S3BucketParams {
 __host__ __device__ inline size_t align128(size_t x) { return (x + 127) & ~(size_t)127; }
 // shared memory: counters [W/2] u32 | staging [kBkStage] u32 | filed lists [kBkStage] u16 |
 // touched passages [kBkTouched] u16 | their first slot [kBkTouched] u16 | per list: first
-// posting in the range [LM] i64, entry prefix [LM + 1] i32.  43.5 KB at LM = 1,024: five CTAs
-// per SM.  (The value rows stay in global memory, read through
-// L1 / L2: holding them in shared memory costs a CTA per SM, and the walk is bound by how many
-// warps are resident, not by those reads.)
+// posting in the range [LM] i64, entry prefix [LM + 1] i32: 43 KB at LM = 1,024, five CTAs per
+// SM.  The value rows and the lists' centroids and lengths stay in global memory, read through
+// L1 / L2: holding them in shared memory costs CTAs per SM, and the walk is bound by how many
+// warps are resident, not by those reads.
 __host__ __device__ inline size_t bucket_smem_bytes(int LM) {
     return align128(4 * (kBkMaxW / 2)) + align128(4 * kBkStage) + align128(2 * kBkStage) + 2 * align128(2 * kBkTouched) +
            align128(8 * (size_t)LM) + align128(4 * (size_t)(LM + 1));
 }
 
-constexpr int kBkCtasPerSm = 5;           // 51 registers per thread
+constexpr int kBkCtasPerSm = 5;           // at most 51 registers per thread (48 used)
 __global__ void __launch_bounds__(kBkThreads, kBkCtasPerSm)
 s3_bucket(S3BucketParams p) {
     extern __shared__ __align__(128) unsigned char bk_smem[];
