@@ -282,9 +282,10 @@ uint64_t ragrt_launch_count(void);
 
 /*
  * Test hook, no counterpart in the reference: launches one warp that waits on an mbarrier
- * nothing arrives on, with the same bounded polling the pipelined kernels use, so that the
- * wait gives up after `polls` polls and sets the device error flag to 3 (read it with
- * ragrt_device_error).  The CUDA context stays usable.
+ * nothing arrives on, with the same bounded wait the pipelined kernels use (polls with a
+ * suspend-time hint, a poll limit, a 2 s global-time deadline and an abort flag shared by the
+ * waiting threads), so that the wait gives up after `polls` polls and sets the device error flag
+ * to 3 (read it with ragrt_device_error).  The CUDA context stays usable.
  */
 int ragrt_selftest_wait_timeout(uint32_t polls, void* stream);
 

@@ -1,6 +1,7 @@
 // selftest.cu -- exercises the bounded-wait error path that every pipelined kernel uses: one
-// warp waits on an mbarrier that nothing arrives on, gives up after `polls` polls, raises the
-// device error flag (value 3) and returns, leaving the context usable.
+// warp waits on an mbarrier that nothing arrives on with tc::mbar_wait_or_abort (suspend-time
+// hinted polls, a poll limit, a global-time deadline and the shared abort flag), gives up after
+// `polls` polls, raises the device error flag (value 3) and returns, leaving the context usable.
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -8,13 +9,18 @@ namespace ragrt {
 
 __global__ void k_wait_timeout(uint32_t polls, int* err) {
     __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
     if (threadIdx.x == 0) {
         tc::mbar_init(&bar, 1);
+        abort_flag = 0;
         tc::mbar_fence_init();
     }
     __syncwarp();
-    const bool ok = tc::mbar_wait_bounded(&bar, 0, polls);   // phase 0 never completes
-    if (!__all_sync(0xFFFFFFFFu, ok) && threadIdx.x == 0) atomicExch(err, 3);
+    // phase 0 never completes: the first lane to reach the limit raises the abort flag, the others
+    // see it within four polls
+    const bool ok = tc::mbar_wait_or_abort(&bar, 0, &abort_flag, polls);
+    __syncwarp();
+    if (!__all_sync(0xFFFFFFFFu, ok) && threadIdx.x == 0) atomicExch(err, abort_flag == 1 ? 3 : 4);
 }
 
 }  // namespace ragrt
