@@ -39,7 +39,7 @@ constexpr uint32_t kColA2 = 64;                       // inside an A slot
 constexpr uint32_t kColD = 256;                       // D slot d: columns 256 + 64 d: 32 dots, D2 (16)
 constexpr uint32_t kColNorm = 32;                     // inside a D slot
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kWaitLimit = 1u << 24;             // polls before a wait is declared failed
+constexpr uint32_t kWaitLimit = 1u << 24;             // polls (or 2 s) before a wait is declared failed
 constexpr int kLutCopies = 16;
 constexpr int kRowStride = 272;                       // staging row: 256 B + 16 B padding (conflict free)
 constexpr int kStageBytes = 32 * kRowStride + 32 * 32;
