@@ -217,19 +217,23 @@ __device__ __noinline__ uint64_t s2_compact(uint64_t* lst, int& n, int kk, bool 
 }
 
 // kTileMax: the pre-pass.  Same GEMM; the epilogue only records, per row and 128-centroid
-// tile, RN16(max acc - eps), a lower bound of the tile's best fp16 score.  Both passes run two
-// epilogue warp sets of four (one warp per lane quadrant): the pre-pass's sets take alternate
-// tiles; the selecting pass's sets take every tile and split each quadrant's 32 rows, set s
-// admitting candidates for rows 16 s .. 16 s + 15 only, so that each row list has one owner.
+// tile, RN16(max acc - eps), a lower bound of the tile's best fp16 score.  A pre-pass CTA covers
+// two 128-row blocks, so that every centroid tile it streams serves 256 rows (the pass is bound
+// by that stream out of L2): per tile two accumulators, one per row block, in two tile buffers.
+// Both passes run two epilogue warp sets of four (one warp per lane quadrant), and both sets
+// take every tile: in the pre-pass set s drains row block s; in the selecting pass the sets
+// split each quadrant's 32 rows, set s admitting candidates for rows 16 s .. 16 s + 15 only, so
+// that each row list has one owner.
 template <bool kTileMax>
 __global__ void __launch_bounds__(kS2TcThreads, 1)
 s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmC, S2TcParams p) {
-    constexpr int kSets = kTileMax ? 2 : 1;          // tile sets
+    constexpr int kRB = kTileMax ? 2 : 1;            // 128-row blocks per CTA
+    constexpr int kTB = kAccBufs / kRB;              // tile buffers in tensor memory
     extern __shared__ uint8_t s2_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)s2_raw + 1023) & ~(uintptr_t)1023);
     const int S = p.stages, kk = p.kk;
     uint8_t* sA = sm;
-    uint8_t* sB = sm + kQTileBytes;
+    uint8_t* sB = sm + kRB * kQTileBytes;
     uint64_t* lists = reinterpret_cast<uint64_t*>(sB + (size_t)S * kTileBytes);    // [128 rows][kListCap]
     float* scratch = reinterpret_cast<float*>(lists + (kTileMax ? 0 : (size_t)kListCap * kQM));  // [128][33]
     uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + (kTileMax ? 0 : kQM * 33));   // 8-byte aligned
@@ -251,10 +255,10 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     if (threadIdx.x == 0) {
         tc::mbar_init(fullA, 1);
         for (int s = 0; s < S; ++s) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
-        // a tile is drained by one warp set (pre-pass) or by both (selecting pass)
-        for (int b = 0; b < kAccBufs; ++b) {
+        // a tile buffer is drained by both warp sets
+        for (int b = 0; b < kTB; ++b) {
             tc::mbar_init(accf + b, 1);
-            tc::mbar_init(acce + b, kTileMax ? 4 : 8);
+            tc::mbar_init(acce + b, 8);
         }
         *abort = 0;
         tc::mbar_fence_init();
@@ -271,9 +275,12 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0 && ntiles > 0) {
-            tc::mbar_arrive_expect_tx(fullA, kQTileBytes);
-            tc::tma_load_2d(sA, &tmQ, 0, rb * kQM, fullA);
-            tc::tma_load_2d(sA + kQTileBytes / 2, &tmQ, 64, rb * kQM, fullA);
+            tc::mbar_arrive_expect_tx(fullA, kRB * kQTileBytes);
+#pragma unroll
+            for (int j = 0; j < kRB; ++j) {           // rows past the end are zero-filled
+                tc::tma_load_2d(sA + j * kQTileBytes, &tmQ, 0, (rb * kRB + j) * kQM, fullA);
+                tc::tma_load_2d(sA + j * kQTileBytes + kQTileBytes / 2, &tmQ, 64, (rb * kRB + j) * kQM, fullA);
+            }
             for (int i = 0; i < ntiles; ++i) {
                 const int s = i % S;
                 if (i >= S && !tc::mbar_wait_or_abort(empty + s, ((i / S) - 1) & 1, abort, kS2WaitLimit)) break;
@@ -290,18 +297,21 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
             const uint32_t aBase = tc::smem_u32(sA);
             bool ok = tc::mbar_wait_or_abort(fullA, 0, abort, kS2WaitLimit);
             for (int i = 0; ok && i < ntiles; ++i) {
-                const int s = i % S, b = i % kAccBufs;
+                const int s = i % S, b = i % kTB;
                 if (!tc::mbar_wait_or_abort(full + s, (i / S) & 1, abort, kS2WaitLimit)) break;
-                if (i >= kAccBufs && !tc::mbar_wait_or_abort(acce + b, ((i / kAccBufs) - 1) & 1, abort, kS2WaitLimit))
+                if (i >= kTB && !tc::mbar_wait_or_abort(acce + b, ((i / kTB) - 1) & 1, abort, kS2WaitLimit))
                     break;
                 tc::fence_after();
                 const uint32_t bBase = tc::smem_u32(sB + (size_t)s * kTileBytes);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const uint32_t koffA = (uint32_t)((k >> 2) * (kQTileBytes / 2) + (k & 3) * 32);
-                    const uint32_t koffB = (uint32_t)((k >> 2) * (kTileBytes / 2) + (k & 3) * 32);
-                    tc::mma_ss(tbase + (uint32_t)(b * kCN), tc::sw128_kmajor_desc(aBase + koffA),
-                               tc::sw128_kmajor_desc(bBase + koffB), idesc, k > 0);
+                for (int j = 0; j < kRB; ++j) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const uint32_t koffA = (uint32_t)(j * kQTileBytes + (k >> 2) * (kQTileBytes / 2) + (k & 3) * 32);
+                        const uint32_t koffB = (uint32_t)((k >> 2) * (kTileBytes / 2) + (k & 3) * 32);
+                        tc::mma_ss(tbase + (uint32_t)((b * kRB + j) * kCN), tc::sw128_kmajor_desc(aBase + koffA),
+                                   tc::sw128_kmajor_desc(bBase + koffB), idesc, k > 0);
+                    }
                 }
                 tc::mma_commit(empty + s);
                 tc::mma_commit(accf + b);
@@ -316,10 +326,10 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         // superset keys and compacted (bitonic sort + trim) warp-wide.
         const int quad = warp & 3;
         const int wset = (warp - 2) >> 2;               // warp set 0 or 1
-        const int set = kTileMax ? wset : 0;            // this warp's tiles: set, set + kSets, ...
+        const int blk = kTileMax ? wset : 0;            // this warp's row block in the CTA
         const bool own = kTileMax || (lane >> 4) == wset;  // selecting pass: this lane's row is this warp's
         const int r = quad * 32 + lane;
-        const int grow = rb * kQM + r;
+        const int grow = (rb * kRB + blk) * kQM + r;
         const int qb = grow / p.rows, tok = grow % p.rows;
         const bool valid = grow < p.rows_total && tok < (p.ntok ? min(p.ntok[qb], p.rows) : p.rows);
         const __half* qrow = p.Q + (int64_t)(valid ? grow : 0) * kDim;
@@ -344,15 +354,15 @@ s2_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorM
         unsigned long long* gT = p.gthr + (valid ? grow : 0);
         uint64_t* wl = lists + (size_t)quad * 32 * kListCap;        // the warp's 32 row lists
         float* sc = scratch + (quad * 32 + lane) * 33;              // this lane's staged chunk scores
-        for (int i = set; i < ntiles; i += kSets) {
-            const int b = i % kAccBufs;
+        for (int i = 0; i < ntiles; ++i) {
+            const int b = i % kTB;
             // other slices' progress on this row (issued before the wait to hide its latency)
             const unsigned long long g =
                 (!kTileMax && valid) ? *reinterpret_cast<volatile unsigned long long*>(gT) : 0ull;
-            const bool ok = tc::mbar_wait_or_abort(accf + b, (i / kAccBufs) & 1, abort, kS2WaitLimit);
+            const bool ok = tc::mbar_wait_or_abort(accf + b, (i / kTB) & 1, abort, kS2WaitLimit);
             if (!__all_sync(0xFFFFFFFFu, ok)) break;          // warp-uniform: tcgen05.ld is warp-collective
             tc::fence_after();
-            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kCN);
+            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + (uint32_t)((b * kRB + blk) * kCN);
             const int c0 = (t0 + i) * kCN;
             if constexpr (kTileMax) {
                 uint32_t v[4][32];
@@ -699,21 +709,27 @@ static int make_map(CUtensorMap* m, const void* base, int64_t rows) {
 
 static size_t s2_tc_smem(bool tilemax, int stages) {
     const size_t lists = tilemax ? 0 : (size_t)kListCap * kQM * 8 + (size_t)kQM * 33 * 4;
-    return 1024 + kQTileBytes + (size_t)stages * kTileBytes + lists + 8 * (1 + 2 * stages + 2 * kAccBufs) + 16;
+    return 1024 + (tilemax ? 2 : 1) * (size_t)kQTileBytes + (size_t)stages * kTileBytes + lists +
+           8 * (1 + 2 * stages + 2 * kAccBufs) + 16;
 }
 
 bool s2_tc_supported(int kk, int64_t rows_total) {
     return rows_total >= kQM && kk < kListCap && s2_tc_smem(false, 2) <= 227 * 1024;
 }
 
-void s2_tc_plan(int B, int rows, int NC, int& nslices, int& tiles_per_slice) {
-    const int rbs = (int)ceil_div((int64_t)B * rows, kQM);
+// Centroid slices for CTAs of `cta_rows` query rows (the selecting pass: 128; the pre-pass: 256).
+static void s2_tc_plan_rows(int B, int rows, int NC, int cta_rows, int& nslices, int& tiles_per_slice) {
+    const int rbs = (int)ceil_div((int64_t)B * rows, cta_rows);
     const int tiles = (int)ceil_div(NC, kCN);
     const int sms = num_sms();
     // one wave of CTAs: every extra slice re-pays the top-k warm-up of each row
     const int best = (int)std::max<int64_t>(1, std::min<int64_t>({32, (int64_t)tiles, sms / std::max(1, rbs)}));
     tiles_per_slice = (int)ceil_div(tiles, best);
     nslices = (int)ceil_div(tiles, tiles_per_slice);
+}
+
+void s2_tc_plan(int B, int rows, int NC, int& nslices, int& tiles_per_slice) {
+    s2_tc_plan_rows(B, rows, NC, kQM, nslices, tiles_per_slice);
 }
 
 size_t s2_tc_partial_bytes(int B, int rows, int NC, int kk) {
@@ -736,8 +752,11 @@ int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __hal
     int stages = 4;
     while (stages > 2 && s2_tc_smem(false, stages) > 227 * 1024) --stages;
     const size_t smem = s2_tc_smem(false, stages);
-    const int pre_stages = 6;                     // the pre-pass keeps no lists: a deeper ring fits
+    int pre_stages = 6;                           // the pre-pass keeps no lists: a deeper ring fits
+    while (pre_stages > 2 && s2_tc_smem(true, pre_stages) > 227 * 1024) --pre_stages;
     const size_t pre_smem = s2_tc_smem(true, pre_stages);
+    int pre_ns, pre_tps;
+    s2_tc_plan_rows(B, rows, NC, 2 * kQM, pre_ns, pre_tps);
     unsigned long long* gthr = reinterpret_cast<unsigned long long*>(
         partial + (size_t)B * nslices * rows * kListCap);
     const int tiles_total = (int)ceil_div(NC, kCN);
@@ -746,11 +765,14 @@ int s2_tc_run(const __half* Q, const int32_t* ntok, int B, int rows, const __hal
                  nslices, stages};
     S2TcParams pp = p;
     pp.stages = pre_stages;
+    pp.tiles_per_slice = pre_tps;
+    pp.nslices = pre_ns;
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pre_smem));
     RAGRT_CUDA_TRY(cudaFuncSetAttribute(s2_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(nslices, (unsigned)ceil_div((int64_t)B * rows, kQM));
+    dim3 pre_grid(pre_ns, (unsigned)ceil_div((int64_t)B * rows, 2 * kQM));
     // pre-pass: per-row tile bounds -> seeded admission keys; then the selecting pass
-    s2_tc<true><<<grid, kS2TcThreads, pre_smem, stream>>>(tmQ, tmC, pp);
+    s2_tc<true><<<pre_grid, kS2TcThreads, pre_smem, stream>>>(tmQ, tmC, pp);
     RAGRT_LAUNCH_CHECK();
     s2_seed_threshold<<<(unsigned)ceil_div((int64_t)B * rows * 32, 256), 256, 0, stream>>>(tilemax, tiles_total,
                                                                                           B * rows, kk, gthr);
