@@ -3,13 +3,14 @@
 // epilogue.  The reference computes Q @ C^T with a cuBLAS fp16 GEMM and torch.topk per
 // query (src/weft_prep.py:32-47); the full [32, NC] score matrix is never materialised here.
 //
-// CTA = 128 query rows (4 queries of 32 tokens) x one slice of the centroids.
+// CTA = 128 query rows (4 queries of 32 tokens; the pre-pass below: two such row blocks) x one
+// slice of the centroids.
 //   warp 0 : TMA producer -- the 128 x 128 query tile once, then 128-centroid x 128-dim
 //            tiles of C through a ring of shared-memory stages (128-byte swizzle, K-major)
-//   warp 1 : MMA issuer -- per tile 8 x tcgen05.mma (M=128, N=128, K=16) into one of four
+//   warp 1 : MMA issuer -- per tile 8 x tcgen05.mma (M=128, N=128, K=16) per row block into
 //            tensor-memory accumulators (4 x 128 columns = all 512)
-//   warps 2-5 (epilogue, one per tensor-memory lane quadrant): drain the accumulator with
-//            tcgen05.ld and release it.  Each fp32 accumulation brackets the exact fp16 score:
+//   warps 2-9 (epilogue, two sets of four, one warp per tensor-memory lane quadrant): drain
+//            the accumulator with tcgen05.ld and release it.  Each fp32 accumulation brackets the exact fp16 score:
 //            lo = RN16(acc - eps) <= RN16(exact) <= hi = RN16(acc + eps) (s2_common.cuh).
 //            Lane l filters its row's 128 scores against the row's admission key Te (a
 //            lower bound on the row's final kk-th key); rows with survivors in a 32-column
