@@ -10,8 +10,9 @@
 //   warp 1 : MMA issuer -- per tile 8 x tcgen05.mma (M=128, N=128, K=16) per row block into
 //            tensor-memory accumulators (4 x 128 columns = all 512)
 //   warps 2-9 (epilogue, two sets of four, one warp per tensor-memory lane quadrant): drain
-//            the accumulator with tcgen05.ld and release it.  Each fp32 accumulation brackets the exact fp16 score:
-//            lo = RN16(acc - eps) <= RN16(exact) <= hi = RN16(acc + eps) (s2_common.cuh).
+//            the accumulator with tcgen05.ld and release it.  Each fp32 accumulation brackets
+//            the exact fp16 score: lo = RN16(acc - eps) <= RN16(exact) <= hi = RN16(acc + eps)
+//            (s2_common.cuh).
 //            Lane l filters its row's 128 scores against the row's admission key Te (a
 //            lower bound on the row's final kk-th key); rows with survivors in a 32-column
 //            chunk are then taken one at a time by the whole warp, lane = centroid, which
